@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""Benchmark of the MuSc scoring hot path on B200: pool images scored per second.
+
+Workload: a pool of N = 100 images, 4 hooked layers x
+radii {1, 3, 5}, 1369 patches x 1024 channels fp32 tokens from the seeded
+prototype-mixture generator (MVTec is not available; the generator stands in
+for it).  One step = the whole scoring path for one pool: LNAMD of 4 layers
+(3 radii each), 12 MSM banks (bank prep, fused distance/min GEMM, interval
+average) and the score reduction (maps, up-sampled image maxima).
+
+* ``value``  -- N / step time with the tokens already resident in HBM
+  (2.24 GB of inputs per step, far above the 126 MB L2, so no flush is needed).
+* ``e2e``    -- the same through the public API with host buffers: pinned
+  host tokens copied in and maps / image maxima copied out every step.
+* ``roofline`` -- the dominant kernel (nearest_kernel) timed live with CUDA
+  events on its stream: algorithmic flops 2*C*P^2*N*(N-1) per launch.
+* ``cpu_baseline`` -- the numpy oracle of the reference's ``original`` path on
+  the host cores, on a bounded sample, scaled to images/s.
+
+``--gpus N`` under torchrun: rank r scores query images [r*ceil(N/G), ...)
+against the whole pool (banks all-gathered over NCCL); the time is the max
+over ranks and ``value`` counts the whole pool (strong scaling).
+``--impl reference`` times the CPU oracle port of the reference path instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / 'musc-gpu_b200'))
+
+N_POOL = 100
+N_LAYERS = 4
+RADII = (1, 3, 5)
+SIDE = 37
+C = 1024
+P = SIDE * SIDE
+METRIC = 'pool images scored/sec (1369x1024 patches, 4 layers x 3 radii)'
+UNIT = 'images/s'
+MSM_FLOP_PER_BANK = 2.0 * C * P * P * N_POOL * (N_POOL - 1)   # directed, SURVEY 8(d)
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=5)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--pool', type=int, default=N_POOL)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    return ap.parse_args()
+
+
+def _peaks():
+    try:
+        return json.loads((REPO / 'MEASURED_PEAKS.json').read_text()), 'measured'
+    except Exception:
+        return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
+
+
+def _traffic():
+    """DRAM bytes per nearest_kernel launch from the committed ncu summary (or None)."""
+    f = REPO / 'profiles' / 'nearest_kernel_traffic.json'
+    try:
+        d = json.loads(f.read_text())
+        return d.get('bytes_per_launch_config2')
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--id={self.gpu}', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '200'], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.file is None:
+            return None
+        try:
+            lines = [l.strip() for l in Path(self.file.name).read_text().splitlines() if l.strip()]
+            os.unlink(self.file.name)
+        except Exception:
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for l in lines:
+            f = [x.strip() for x in l.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ----------------------------------------------------------------- CPU oracle
+class CpuSample:
+    """Time the oracle (the reference's original path restated in numpy) on a bounded sample.
+
+    Sample: LNAMD (r = 1, 3, 5) of 2 images of one layer, and the MSM rows of
+    one query image against the pool for one (layer, radius) bank.  Scaled to
+    a pool image: 4 layers of LNAMD + 12 banks of MSM rows.  Setup (the
+    pool's tokens and its r=3 bank) is untimed.
+    """
+
+    def __init__(self, pool: int, seed: int = 1):
+        import torch
+        from musc_b200.synthetic import prototype_mixture_layer
+        from oracle import lnamd as olnamd
+        from oracle import msm as omsm
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.olnamd, self.omsm = olnamd, omsm
+        self.tokens = prototype_mixture_layer(pool, generator=torch.Generator().manual_seed(seed)).numpy()
+        self.z = olnamd.bank(self.tokens, 3)
+        self.a, self.b = omsm.trimmed_ranks(pool)
+
+    def per_image_seconds(self) -> float:
+        t0 = time.perf_counter()
+        for r in RADII:
+            self.olnamd.bank(self.tokens[:2], r)
+        t_lnamd = (time.perf_counter() - t0) / 2          # per image, 3 radii, one layer
+        t0 = time.perf_counter()
+        self.omsm.interval_average(self.omsm.nearest_minima(self.z, 0), self.a, self.b)
+        t_msm = time.perf_counter() - t0                  # one query image, one bank
+        return N_LAYERS * t_lnamd + N_LAYERS * len(RADII) * t_msm
+
+
+CPU_SAMPLE_TEXT = ('numpy oracle of the reference original path: LNAMD r{1,3,5} of 2 images x 1 layer + '
+                   'MSM rows of 1 query image x 1 bank vs the whole pool, scaled to 4 layers x 12 banks '
+                   'per pool image')
+
+
+def run_reference(args):
+    """``--impl reference``: the oracle port of the reference's CPU path, rank 0 only."""
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(REPO))
+    cores = os.cpu_count() or 1
+    sample = CpuSample(args.pool)
+    for _ in range(max(args.warmup, 0)):
+        sample.per_image_seconds()
+    times = [sample.per_image_seconds() for _ in range(args.steps)]
+    per_image = statistics.median(times)
+    value = 1.0 / per_image
+    line = {
+        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': per_image * args.pool * 1e3, 'higher_is_better': True,
+        'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'impl': 'reference',
+        'config': {'workload': f'config2: pool N={args.pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32',
+                   'global_batch': args.pool, 'l2': 'inputs larger than L2'},
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                         'sample': CPU_SAMPLE_TEXT},
+        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arm
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    from musc_b200 import ops, pipeline
+    from musc_b200.synthetic import prototype_mixture
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if world != args.gpus:
+        raise SystemExit(f'--gpus {args.gpus} but WORLD_SIZE={world}')
+    torch.cuda.set_device(local_rank)
+    dev = torch.device('cuda', local_rank)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+        group = dist.group.WORLD
+
+    pool = args.pool
+    first, end, _ = pipeline.shard_range(pool, world, rank)
+    host = [t[first:end].contiguous().pin_memory() for t in prototype_mixture(pool, N_LAYERS, C, SIDE, seed=0)]
+    tokens = [h.to(dev, non_blocking=True) for h in host]
+    torch.cuda.synchronize()
+
+    # Instrument the dominant kernel's launches with events on its stream.
+    near_events = []
+    orig_nearest = ops.nearest
+
+    def timed_nearest(*a, **k):
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        out = orig_nearest(*a, **k)
+        e1.record(s)
+        near_events.append((e0, e1))
+        return out
+
+    class Kernels:
+        pass
+    kern = Kernels()
+    for name in ('lnamd', 'lnamd_super_fast', 'prep_bank', 'trimmed_mean', 'score_maps', 'trimmed_ranks'):
+        setattr(kern, name, getattr(ops, name))
+    kern.nearest = timed_nearest
+
+    def step():
+        return pipeline.score_pool(tokens, n_images=pool, radii=RADII, group=group, kernels=kern)
+
+    def barrier():
+        if group is not None:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    near_events.clear()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    near_ms = [a.elapsed_time(b) for a, b in near_events]
+
+    # e2e: host tokens in, maps and image maxima out, every step.
+    dev_buf = [torch.empty_like(t) for t in tokens]
+    h2d = sum(h.numel() * h.element_size() for h in host)
+
+    def e2e_step():
+        for h, d in zip(host, dev_buf):
+            d.copy_(h, non_blocking=True)
+        res = pipeline.score_pool(dev_buf, n_images=pool, radii=RADII, group=group)
+        maps, mx = pipeline.gather_pool(res, group)
+        if rank == 0:
+            return maps.cpu(), mx.cpu()
+        return None
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    d2h = 0
+    for _ in range(args.steps):
+        out = e2e_step()
+        if out is not None:
+            d2h = sum(o.numel() * o.element_size() for o in out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    stats = torch.tensor([elapsed_ms, e2e_ms, sum(near_ms) / max(len(near_ms), 1)], dtype=torch.float64,
+                         device=dev)
+    if group is not None:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms, near_avg_ms = stats.tolist()
+
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        ms_per_step = elapsed_ms / args.steps
+        value = pool / (ms_per_step / 1e3)
+        n_local = end - first
+        q_rows = n_local * P
+        achieved_tflops = MSM_FLOP_PER_BANK * (n_local / pool) / (near_avg_ms / 1e3) / 1e12
+        # executed tensor-core work: 3 MMA passes over whole 128 x 256 tiles
+        tiles_m = math.ceil(q_rows / 128)
+        tiles_n = math.ceil(pool * P / 256)
+        mma_tflops = 3 * 2.0 * tiles_m * 128 * tiles_n * 256 * C / (near_avg_ms / 1e3) / 1e12
+        peak = peaks.get('bf16_tflops_sustained', peaks.get('bf16_tflops'))
+        launches_per_step = N_LAYERS * 2 + len(RADII) * N_LAYERS * (4 + (1 if world > 1 else 0)) + 1
+        line = {
+            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'config': {'workload': f'config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 '
+                                   'prototype-mixture tokens resident in HBM',
+                       'global_batch': pool, 'seq_len': P, 'parallelism': f'query-shard{world}',
+                       'l2': 'inputs larger than L2 (2.24 GB tokens per step); no flush'},
+            'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
+                    'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
+            'roofline': {'kernel': 'nearest_kernel', 'bound': 'tensor', 'achieved': achieved_tflops,
+                         'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved_tflops / peak,
+                         'traffic': _traffic(),
+                         'peak_kind': f'{peak_kind} bf16 sustained (kernel timed inside a long step)',
+                         'mma_executed_tflops': mma_tflops, 'mma_frac': mma_tflops / peak,
+                         'mma_kind': 'kind::f16 (fp16 split hi/lo, 3 passes)',
+                         'launch_ms': near_avg_ms},
+            'gpu_launches': launches_per_step * args.steps,
+            'clocks': clocks.summary(),
+        }
+        if not args.no_cpu_baseline:
+            sys.path.insert(0, str(REPO))
+            sample = CpuSample(pool)
+            sample.per_image_seconds()
+            per_image = statistics.median(sample.per_image_seconds() for _ in range(3))
+            line['cpu_baseline'] = {'value': 1.0 / per_image, 'unit': UNIT, 'cores': os.cpu_count(),
+                                    'kind': 'port', 'sample': CPU_SAMPLE_TEXT}
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main():
+    args = _args()
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,153 @@
+/*
+ * musc_b200.h -- C ABI of the B200 (sm_100a) MuSc scoring library.
+ *
+ * The library replaces the reference's scoring hot path: LNAMD neighbourhood
+ * aggregation, MSM mutual scoring with the interval average, the score
+ * reduction, and the ViT block softmax attention.  Each entry point names the
+ * reference interface it replaces (paths relative to the MuSc checkout).
+ *
+ * Conventions (all entry points):
+ *   - Return an int status: MUSC_B200_OK (0) or one of the error codes below.
+ *     musc_b200_last_error() returns a thread-local message for the last
+ *     failure on the calling thread.  No exception crosses the ABI.
+ *   - Every tensor argument is caller-owned device memory of the current
+ *     device; the library never allocates or frees it.  Scratch memory comes
+ *     from a caller-provided workspace sized by the matching *_bytes query.
+ *   - Work is enqueued on `stream` (a cudaStream_t; 0 = legacy default
+ *     stream) and is asynchronous to the host, like the reference's launches
+ *     on torch's current stream (models/modules/_cuda_runtime.py:95-100).
+ *   - Entry points are stateless and reentrant per stream.
+ *   - The device must be sm_100 (B200); anything else returns
+ *     MUSC_B200_ERR_DEVICE.  There is no CPU fallback.
+ */
+#ifndef MUSC_B200_H
+#define MUSC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* musc_b200_stream; /* same type as cudaStream_t */
+
+enum musc_b200_status {
+  MUSC_B200_OK = 0,
+  MUSC_B200_ERR_INVALID = 1,   /* shape / dtype / rank contract: the reference raises ValueError
+                                  (models/modules/_MSM_gpu.py:702-711, _backend.py:6-7) */
+  MUSC_B200_ERR_CUDA = 2,      /* CUDA runtime or driver failure: the reference raises RuntimeError
+                                  (models/modules/_cuda_runtime.py:47-55) */
+  MUSC_B200_ERR_DEVICE = 3,    /* current device is not sm_100 */
+  MUSC_B200_ERR_WORKSPACE = 4, /* workspace smaller than the *_bytes query */
+  MUSC_B200_ERR_TIMEOUT = 5    /* a device-side bounded wait expired (reported by
+                                  musc_b200_take_device_error) */
+};
+
+enum musc_b200_dtype { MUSC_B200_F32 = 0, MUSC_B200_F16 = 1, MUSC_B200_BF16 = 2 };
+
+/* ABI version of this header (bumped on any signature change). */
+int musc_b200_abi_version(void);
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* musc_b200_last_error(void);
+
+/* Reads and clears the device-side error word of the current device
+ * (MUSC_B200_OK or MUSC_B200_ERR_TIMEOUT).  Synchronises the device. */
+int musc_b200_take_device_error(int* code);
+
+/* ------------------------------------------------------------------------
+ * LNAMD
+ * Replaces LNAMD._embed (models/modules/_LNAMD.py:72-129), its direct-pool
+ * form aggregate_features (models/modules/_encoder_gpu.py:14-42) with the
+ * radius cache (models/modules/_aggregation_cache.py:15-58), and the
+ * L2 normalisation of models/musc.py:238.
+ *
+ * tokens: [n_images][tokens_per_image][channels] of `dtype`; token 0 is the
+ *         CLS token and is skipped; tokens_per_image - 1 = side*side.
+ * For each requested radius r in {1, 3, 5}: LayerNorm over the whole
+ * (channels, side, side) image (weight 1, bias 0, eps 1e-5, biased variance),
+ * then the zero-padded r x r mean with divisor r^2, then (l2_normalize != 0)
+ * division by the per-patch L2 norm over channels.
+ * out[i] receives radius radii[i] at
+ *     out[i][image * out_image_stride + patch * out_patch_stride + channel]
+ * (float32), so the reference's (B, P, layers, C) stack and a contiguous
+ * (N, P, C) scoring bank are both expressible.  channels % 4 == 0,
+ * channels <= 2048, strides % 4 == 0.
+ * ---------------------------------------------------------------------- */
+size_t musc_b200_lnamd_workspace_bytes(int n_images);
+
+int musc_b200_lnamd(const void* tokens, int dtype, int n_images, int tokens_per_image,
+                    int channels, int n_radii, const int* radii, float* const* out,
+                    long long out_image_stride, long long out_patch_stride, int l2_normalize,
+                    void* workspace, size_t workspace_bytes, musc_b200_stream stream);
+
+/* Super-fast profile: r = 3 LNAMD on the side x side grid, then
+ * adaptive_avg_pool2d to out_side x out_side (fp32), then optional L2
+ * normalisation.  Replaces SuperFastAggregation.__call__
+ * (models/modules/_super_fast.py:17-27) followed by models/musc.py:238. */
+int musc_b200_lnamd_super_fast(const void* tokens, int dtype, int n_images,
+                               int tokens_per_image, int channels, int out_side, float* out,
+                               long long out_image_stride, long long out_patch_stride,
+                               int l2_normalize, void* workspace, size_t workspace_bytes,
+                               musc_b200_stream stream);
+
+/* ------------------------------------------------------------------------
+ * MSM mutual scoring
+ * Replaces models/modules/_MSM.py:10-59 (original) and
+ * models/modules/_MSM_gpu.py:701-830 (the reference GPU driver).
+ *
+ * A "bank" is the tensor-core operand form of a block of feature rows
+ * z[rows][channels] (fp32): each row scaled by a power of two and split into
+ * fp16 hi + lo halves, plus fp32 squared norms and the inverse scales.
+ * ---------------------------------------------------------------------- */
+size_t musc_b200_bank_bytes(long long rows, int channels);
+
+/* z: [rows][channels] fp32, channels % 8 == 0.  bank: >= bank_bytes. */
+int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
+                        size_t bank_bytes, musc_b200_stream stream);
+
+/* Nearest-patch minima, squared: for every query row q (global row
+ * query_first_row + q, image (query_first_row + q) / patches_per_image) and
+ * every reference image j != that image,
+ *   nearest_sq[j * query_rows + q] = min over the patches p of image j of
+ *                                    |z_q - z_p|^2   (clamped at 0),
+ * and FLT_MAX in the query's own image slot (_MSM_gpu.py:202).  This is
+ * _MSM.py:16-17 before the square root.  The reference bank holds rows
+ * [0, ref_rows) = images [0, ref_rows / patches_per_image).
+ * n_images = ref_rows / patches_per_image.  tcgen05 split-fp16 GEMM with the
+ * min fused into the epilogue; the distance matrix never reaches memory. */
+int musc_b200_nearest(const void* query_bank, long long query_rows, long long query_first_row,
+                      const void* ref_bank, long long ref_rows, int channels,
+                      int patches_per_image, float* nearest_sq, musc_b200_stream stream);
+
+/* Interval average: scores[q] = mean of ranks [rank_lo, rank_hi) of
+ * sqrt(nearest_sq[:, q]) over the n_images - 1 other images, in float32,
+ * stored as float64 (_MSM.py:19-30).  0 <= rank_lo < rank_hi <= n_images-1. */
+int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
+                           int rank_lo, int rank_hi, double* scores, musc_b200_stream stream);
+
+/* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64.
+ * The workspace holds the bank and the nearest table. */
+size_t musc_b200_msm_workspace_bytes(int n, int p, int c);
+
+int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi,
+                  double* scores, void* workspace, size_t workspace_bytes,
+                  musc_b200_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Score reduction: models/musc.py:259-288.
+ * scores: [n_radii][n_layers][n][side*side] float64.  maps[n][side*side] =
+ * mean over layers, then over radii; image_max[n] = max of the bilinear
+ * (align_corners=True) up-sampling of each map to image_size^2; upsampled
+ * (nullable) receives that [n][image_size][image_size] map.
+ * ---------------------------------------------------------------------- */
+int musc_b200_score_maps(const double* scores, int n_radii, int n_layers, int n, int side,
+                         int image_size, double* maps, double* image_max, double* upsampled,
+                         musc_b200_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUSC_B200_H */

@@ -1,0 +1,674 @@
+// MSM mutual scoring.
+//
+// Reference: compute_scores_fast / MSM (models/modules/_MSM.py:10-59) and the
+// reference GPU driver models/modules/_MSM_gpu.py:701-830.
+//
+// Pipeline for one (layer, radius) bank z[N*P][C] fp32:
+//   1. prep_bank_kernel: per row, a power-of-two scale 2^k putting max|z|
+//      in [2^14, 2^15), the split z*2^k = hi + lo with hi = fp16(z*2^k) and
+//      lo = fp16(z*2^k - hi) (together ~22 significant bits, fp32-class
+//      accuracy), the fp32 squared norm (float64 accumulation) and 2^-k.
+//   2. nearest_kernel: persistent, warp-specialised tcgen05 GEMM.  Each tile
+//      is 128 query rows x 256 reference rows; per 32-wide K slice TMA brings
+//      A_hi, A_lo, B_hi, B_lo (48 KB) into a 4-deep shared-memory ring, and one
+//      thread issues hi*hi + hi*lo + lo*hi (6 MMAs of 128x256x16) into a
+//      fp32 TMEM accumulator (2 x 256 columns, double-buffered).  Four
+//      epilogue warps read the accumulator (tcgen05.ld), form
+//      d^2 = |q|^2 + |r|^2 - 2 q.r, keep a running minimum per reference
+//      image segment and atomically lower nearest_sq[image][row].  The
+//      N*P x N*P distance matrix never reaches memory.
+//   3. trimmed_mean_kernel: per query row, the sum of the smallest m
+//      distances by a binary search on the order-preserving bit pattern of
+//      the squared minima (exact threshold, ties handled by count), for
+//      m = rank_hi and rank_lo; score = mean of ranks [rank_lo, rank_hi)
+//      rounded to fp32 like the reference's fp32 mean, stored as float64.
+#include "common.cuh"
+#include "tc.cuh"
+
+#include <cfloat>
+#include <mutex>
+
+namespace musc {
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct BankLayout {
+  size_t hi, lo, norm, inv, total;
+};
+
+static BankLayout bank_layout(long long rows, int channels) {
+  const size_t plane = align_up((size_t)rows * channels * 2, 1024);
+  const size_t vec = align_up((size_t)rows * 4, 1024);
+  return {0, plane, 2 * plane, 2 * plane + vec, 2 * plane + 2 * vec};
+}
+
+// ------------------------------------------------------------------ prep
+constexpr int kPrepWarps = 8;
+
+__global__ void __launch_bounds__(kPrepWarps * 32)
+prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __half* __restrict__ hi,
+                 __half* __restrict__ lo, float* __restrict__ norm2, float* __restrict__ inv_scale) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;  // warp-uniform
+  const float* zr = z + row * channels;
+  float m = 0.f;
+  double ss = 0.0;
+  for (int c = lane * 4; c < channels; c += 128) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
+  m = warp_max(m);
+  ss = warp_sum(ss);
+  int k = 0;
+  if (m > 0.f) {
+    k = 14 - ilogbf(m);
+    k = k > 126 ? 126 : (k < -126 ? -126 : k);
+  }
+  const float s = ldexpf(1.f, k);
+  __half* hr = hi + row * channels;
+  __half* lr = lo + row * channels;
+  for (int c = lane * 4; c < channels; c += 128) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
+    const float x[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+    __half h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      h[e] = __float2half_rn(x[e]);
+      l[e] = __float2half_rn(x[e] - __half2float(h[e]));
+    }
+    uint2 ph, pl;
+    __half2 t;
+    t = __halves2half2(h[0], h[1]); ph.x = *reinterpret_cast<uint32_t*>(&t);
+    t = __halves2half2(h[2], h[3]); ph.y = *reinterpret_cast<uint32_t*>(&t);
+    t = __halves2half2(l[0], l[1]); pl.x = *reinterpret_cast<uint32_t*>(&t);
+    t = __halves2half2(l[2], l[3]); pl.y = *reinterpret_cast<uint32_t*>(&t);
+    *reinterpret_cast<uint2*>(hr + c) = ph;
+    *reinterpret_cast<uint2*>(lr + c) = pl;
+  }
+  if (lane == 0) {
+    norm2[row] = (float)ss;
+    inv_scale[row] = ldexpf(1.f, -k);
+  }
+}
+
+// ------------------------------------------------------------------ nearest
+namespace nearest {
+constexpr int BM = 128;           // query rows per tile (TMEM lanes)
+constexpr int BN = 256;           // reference rows per tile (TMEM columns per accumulator)
+constexpr int BK = 32;            // fp16 elements per K slice = one 64-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;                // 8 KB
+constexpr int B_BYTES = BN * BK * 2;                // 16 KB
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 48 KB
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int GROUP_M = 16;  // m-tiles swept together over the reference columns (L2 reuse)
+constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;  // 4 s per wait
+constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, /*fp16*/ 0);
+
+struct Smem {
+  uint8_t tiles[STAGES][STAGE_BYTES];  // 1024-aligned base
+  float col_norm[BN];
+  float col_w[BN];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[NUM_ACC];
+  uint64_t acc_empty[NUM_ACC];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+
+struct Params {
+  const float* q_norm;
+  const float* q_inv;
+  const float* r_norm;
+  const float* r_inv;
+  unsigned int* nearest;  // [n_images][q_rows] float bits
+  int* err;
+  long long q_rows, r_rows, q_first_row;
+  int patches;  // P
+  int num_kb;
+  int num_m, num_n;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int* m_blk, int* n_blk) {
+  const int group = tile / (GROUP_M * num_n);
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int local = tile - group * GROUP_M * num_n;
+  *m_blk = first_m + local % gm;
+  *n_blk = local / gm;
+}
+
+// Bounded wait: true when the phase completed; false after the time limit
+// (which raises the CTA's abort flag and the device error word) or when
+// another role already aborted.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             int* err) {
+  if (tc::mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  uint32_t iter = 0;
+  while (true) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    if ((++iter & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - start > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        atomicExch(err, MUSC_B200_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void named_sync_epi() {
+  asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+}
+
+// Barrier over the epilogue warps that also ORs `flag` across them, so every
+// epilogue thread takes the same branch afterwards.
+__device__ __forceinline__ bool named_sync_epi_any(int flag) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(res)
+      : "r"(flag), "n"(EPI_WARPS * 32)
+      : "memory");
+  return res != 0;
+}
+
+__device__ __forceinline__ void flush_min(const Params& p, bool row_ok, long long row, int q_img,
+                                          int img, float m) {
+  if (row_ok && img != q_img) {
+    const float v = m > 0.f ? m : 0.f;
+    atomicMin(p.nearest + (long long)img * p.q_rows + row, __float_as_uint(v));
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_constant__ CUtensorMap map_q_lo,
+               const __grid_constant__ CUtensorMap map_r_hi, const __grid_constant__ CUtensorMap map_r_lo,
+               const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(tc::smem_u32(&sm.full[s]), 1);
+      tc::mbar_init(tc::smem_u32(&sm.empty[s]), 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      tc::mbar_init(tc::smem_u32(&sm.acc_full[a]), 1);
+      tc::mbar_init(tc::smem_u32(&sm.acc_empty[a]), EPI_WARPS);
+    }
+    tc::mbar_init(tc::smem_u32(&sm.drain), 1);
+    sm.abort_flag = 0;
+    tc::fence_barrier_init();
+    tc::prefetch_tensormap(&map_q_hi);
+    tc::prefetch_tensormap(&map_q_lo);
+    tc::prefetch_tensormap(&map_r_hi);
+    tc::prefetch_tensormap(&map_r_lo);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem_base = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!wait_bounded(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = tc::smem_u32(&sm.full[stage]);
+          tc::mbar_arrive_expect_tx(full, STAGE_BYTES);
+          const uint32_t base = tc::smem_u32(sm.tiles[stage]);
+          const int kc = kb * BK;
+          tc::tma_load_2d(base, &map_q_hi, kc, m_blk * BM, full);
+          tc::tma_load_2d(base + A_BYTES, &map_q_lo, kc, m_blk * BM, full);
+          tc::tma_load_2d(base + 2 * A_BYTES, &map_r_hi, kc, n_blk * BN, full);
+          tc::tma_load_2d(base + 2 * A_BYTES + B_BYTES, &map_r_lo, kc, n_blk * BN, full);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!issued[s]) continue;
+          const uint64_t start = global_ns();
+          while (!tc::mbar_try_wait(tc::smem_u32(&sm.full[s]), issued_phase[s]) &&
+                 global_ns() - start < WAIT_LIMIT_NS) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!wait_bounded(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!wait_bounded(tc::smem_u32(&sm.full[stage]), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t base = tc::smem_u32(sm.tiles[stage]);
+#pragma unroll
+          for (int k16 = 0; k16 < BK / 16; ++k16) {
+            const uint32_t koff = (uint32_t)(k16 * 32);  // 16 fp16 = 32 bytes along the swizzled row
+            const uint64_t a_hi = tc::desc_k_sw64(base + koff);
+            const uint64_t a_lo = tc::desc_k_sw64(base + A_BYTES + koff);
+            const uint64_t b_hi = tc::desc_k_sw64(base + 2 * A_BYTES + koff);
+            const uint64_t b_lo = tc::desc_k_sw64(base + 2 * A_BYTES + B_BYTES + koff);
+            tc::mma_f16_ss(d_tmem, a_hi, b_hi, IDESC, (kb | k16) != 0 ? 1u : 0u);
+            tc::mma_f16_ss(d_tmem, a_hi, b_lo, IDESC, 1u);
+            tc::mma_f16_ss(d_tmem, a_lo, b_hi, IDESC, 1u);
+          }
+          tc::mma_commit(tc::smem_u32(&sm.empty[stage]));
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        tc::mma_commit(tc::smem_u32(&sm.acc_full[acc]));
+        if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
+      }
+      if (!ok) {
+        // Wait for this thread's MMAs in flight before TMEM is released.
+        tc::mma_commit(tc::smem_u32(&sm.drain));
+        const uint64_t start = global_ns();
+        while (!tc::mbar_try_wait(tc::smem_u32(&sm.drain), 0) && global_ns() - start < WAIT_LIMIT_NS) {
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int et = threadIdx.x - 64;         // 0..127
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int m_blk, n_blk;
+      tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+      const long long n0 = (long long)n_blk * BN;
+      named_sync_epi();  // previous tile's readers are done with col_norm / col_w
+      for (int j = et; j < BN; j += EPI_WARPS * 32) {
+        const long long col = n0 + j;
+        const bool ok = col < p.r_rows;
+        sm.col_norm[j] = ok ? __ldg(p.r_norm + col) : 0.f;
+        sm.col_w[j] = ok ? 2.f * __ldg(p.r_inv + col) : 0.f;
+      }
+      wait_bounded(tc::smem_u32(&sm.acc_full[acc]), acc_phase, abort_flag, p.err);
+      if (named_sync_epi_any(*abort_flag)) break;  // uniform decision across the epilogue warps
+      tc::fence_after_sync();
+
+      const long long row = (long long)m_blk * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.q_rows;
+      const float qn = row_ok ? __ldg(p.q_norm + row) : 0.f;
+      const float qi = row_ok ? __ldg(p.q_inv + row) : 0.f;
+      const int q_img = (int)((p.q_first_row + row) / p.patches);
+      int seg_img = (int)(n0 / p.patches);
+      long long seg_end = (long long)(seg_img + 1) * p.patches;
+      float m = FLT_MAX;
+      bool has = false;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        const long long c0 = n0 + chunk * 32;
+        if (c0 >= p.r_rows) break;
+        uint32_t v[32];
+        tc::tmem_ld_32x32b_x32(tbase + (uint32_t)(chunk * 32), v);
+        tc::tmem_wait_ld();
+        if (c0 + 32 <= seg_end && c0 + 32 <= p.r_rows) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int jj = chunk * 32 + j;
+            const float d2 = fmaf(-__uint_as_float(v[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
+            m = fminf(m, d2);
+          }
+          has = true;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const long long col = c0 + j;
+            if (col < p.r_rows) {
+              if (col >= seg_end) {
+                if (has) flush_min(p, row_ok, row, q_img, seg_img, m);
+                ++seg_img;
+                seg_end += p.patches;
+                m = FLT_MAX;
+                has = false;
+              }
+              const int jj = chunk * 32 + j;
+              const float d2 = fmaf(-__uint_as_float(v[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
+              m = fminf(m, d2);
+              has = true;
+            }
+          }
+        }
+      }
+      if (has) flush_min(p, row_ok, row, q_img, seg_img, m);
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.acc_empty[acc]));
+      if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace nearest
+
+// ------------------------------------------------------------------ fill
+__global__ void fill_u32_kernel(unsigned int* p, long long n, unsigned int v) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+// ------------------------------------------------------------------ trimmed mean
+__device__ __forceinline__ int count_below(const unsigned int* col, int n, int stride, unsigned int t) {
+  int c = 0;
+  for (int j = 0; j < n; ++j) c += col[j * stride] < t ? 1 : 0;
+  return c;
+}
+
+__device__ __forceinline__ double sum_below(const unsigned int* col, int n, int stride, unsigned int t) {
+  double s = 0.0;
+  for (int j = 0; j < n; ++j) {
+    const unsigned int k = col[j * stride];
+    if (k < t) s += (double)sqrtf(__uint_as_float(k));
+  }
+  return s;
+}
+
+// Sum of the m smallest sqrt(values) in the column (keys are non-negative
+// float bit patterns, so integer order is value order).
+__device__ double sum_smallest(const unsigned int* col, int n, int stride, int m, unsigned int kmin,
+                               unsigned int kmax) {
+  if (m <= 0) return 0.0;
+  const int k = m - 1;
+  unsigned int lo = kmin;            // count(< lo) == 0 <= k
+  unsigned int hi = kmax + 1u;       // count(< hi) == n > k
+  while (hi - lo > 1u) {
+    const unsigned int mid = lo + (hi - lo) / 2u;
+    const int c = count_below(col, n, stride, mid);
+    if (c <= k) {
+      lo = mid;
+    } else {
+      hi = mid;
+      if (c == m) return sum_below(col, n, stride, hi);
+    }
+  }
+  // lo is the k-th smallest key: count(< lo) <= k < count(<= lo).
+  const int c_lo = count_below(col, n, stride, lo);
+  return sum_below(col, n, stride, lo) + (double)(m - c_lo) * (double)sqrtf(__uint_as_float(lo));
+}
+
+__global__ void trimmed_mean_kernel(const unsigned int* __restrict__ nearest, long long q_rows, int n,
+                                    int rank_lo, int rank_hi, double* __restrict__ scores) {
+  extern __shared__ unsigned int keys[];  // [n][R], R = blockDim.x
+  const int R = blockDim.x;
+  const long long row0 = (long long)blockIdx.x * R;
+  for (int idx = threadIdx.x; idx < n * R; idx += R) {
+    const int j = idx / R, r = idx - j * R;
+    const long long row = row0 + r;
+    keys[idx] = row < q_rows ? __ldg(nearest + (long long)j * q_rows + row) : 0u;
+  }
+  __syncthreads();
+  const long long row = row0 + threadIdx.x;
+  if (row >= q_rows) return;
+  const unsigned int* col = keys + threadIdx.x;
+  unsigned int kmin = 0xFFFFFFFFu, kmax = 0u;
+  for (int j = 0; j < n; ++j) {
+    const unsigned int k = col[j * R];
+    kmin = k < kmin ? k : kmin;
+    kmax = k > kmax ? k : kmax;
+  }
+  const double hi = sum_smallest(col, n, R, rank_hi, kmin, kmax);
+  const double lo = sum_smallest(col, n, R, rank_lo, kmin, kmax);
+  scores[row] = (double)(float)((hi - lo) / (double)(rank_hi - rank_lo));
+}
+
+// ------------------------------------------------------------------ host helpers
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* fn) {
+  static std::mutex m;
+  static EncodeTiledFn cached = nullptr;
+  std::lock_guard<std::mutex> lock(m);
+  if (!cached) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
+      return fail(MUSC_B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    cached = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  *fn = cached;
+  return MUSC_B200_OK;
+}
+
+// 2-D fp16 plane [rows][channels], box = 32 channels x box_rows, 64-byte swizzle.
+int make_plane_map(CUtensorMap* map, const void* base, long long rows, int channels, int box_rows) {
+  EncodeTiledFn encode;
+  MUSC_TRY(get_encode_fn(&encode));
+  cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
+  cuuint32_t box[2] = {(cuuint32_t)nearest::BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MUSC_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return MUSC_B200_OK;
+}
+
+int check_bank_args(long long rows, int channels) {
+  if (rows <= 0 || channels <= 0) return fail(MUSC_B200_ERR_INVALID, "bank: requires rows > 0, channels > 0");
+  if (channels % 8 != 0) return fail(MUSC_B200_ERR_INVALID, "bank: channels must be a multiple of 8");
+  if (rows > 0x7FFFFFFFLL) return fail(MUSC_B200_ERR_INVALID, "bank: rows must fit in int32");
+  return MUSC_B200_OK;
+}
+
+int trimmed_rows_per_block(int n) {
+  const int budget = smem_optin() - 1024;
+  for (int r = 128; r >= 32; r /= 2)
+    if ((long long)n * r * 4 <= budget) return r;
+  return 0;
+}
+
+}  // namespace
+
+int nearest_launch(const void* query_bank, long long query_rows, long long query_first_row,
+                   const void* ref_bank, long long ref_rows, int channels, int patches,
+                   float* nearest_sq, cudaStream_t s) {
+  const BankLayout ql = bank_layout(query_rows, channels);
+  const BankLayout rl = bank_layout(ref_rows, channels);
+  const uint8_t* qb = static_cast<const uint8_t*>(query_bank);
+  const uint8_t* rb = static_cast<const uint8_t*>(ref_bank);
+  CUtensorMap mqh, mql, mrh, mrl;
+  MUSC_TRY(make_plane_map(&mqh, qb + ql.hi, query_rows, channels, nearest::BM));
+  MUSC_TRY(make_plane_map(&mql, qb + ql.lo, query_rows, channels, nearest::BM));
+  MUSC_TRY(make_plane_map(&mrh, rb + rl.hi, ref_rows, channels, nearest::BN));
+  MUSC_TRY(make_plane_map(&mrl, rb + rl.lo, ref_rows, channels, nearest::BN));
+  const int n_images = (int)(ref_rows / patches);
+  const long long table = (long long)n_images * query_rows;
+  fill_u32_kernel<<<1184, 256, 0, s>>>(reinterpret_cast<unsigned int*>(nearest_sq), table, 0x7F7FFFFFu);
+  MUSC_TRY(check_launch("fill_u32_kernel"));
+  nearest::Params p;
+  p.q_norm = reinterpret_cast<const float*>(qb + ql.norm);
+  p.q_inv = reinterpret_cast<const float*>(qb + ql.inv);
+  p.r_norm = reinterpret_cast<const float*>(rb + rl.norm);
+  p.r_inv = reinterpret_cast<const float*>(rb + rl.inv);
+  p.nearest = reinterpret_cast<unsigned int*>(nearest_sq);
+  p.err = device_error_ptr();
+  if (!p.err) return fail(MUSC_B200_ERR_CUDA, "nearest: device error word unavailable");
+  p.q_rows = query_rows;
+  p.r_rows = ref_rows;
+  p.q_first_row = query_first_row;
+  p.patches = patches;
+  p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
+  p.num_m = (int)((query_rows + nearest::BM - 1) / nearest::BM);
+  p.num_n = (int)((ref_rows + nearest::BN - 1) / nearest::BN);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  MUSC_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !attr_set[dev]) {
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)nearest::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const long long tiles = (long long)p.num_m * p.num_n;
+  if (tiles > 0x7FFFFFFFLL) return fail(MUSC_B200_ERR_INVALID, "nearest: too many tiles");
+  const int grid = (int)std::min<long long>(tiles, sm_count());
+  nearest::nearest_kernel<<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mqh, mql, mrh, mrl, p);
+  return check_launch("nearest_kernel");
+}
+
+int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, int rank_lo, int rank_hi,
+                   double* scores, cudaStream_t s) {
+  const int R = trimmed_rows_per_block(n_images);
+  if (R == 0) return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: too many images for shared memory");
+  const size_t smem = (size_t)n_images * R * 4;
+  MUSC_CUDA(cudaFuncSetAttribute(trimmed_mean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const long long blocks = (query_rows + R - 1) / R;
+  trimmed_mean_kernel<<<(unsigned)blocks, R, smem, s>>>(reinterpret_cast<const unsigned int*>(nearest_sq),
+                                                        query_rows, n_images, rank_lo, rank_hi, scores);
+  return check_launch("trimmed_mean_kernel");
+}
+
+}  // namespace musc
+
+using namespace musc;
+
+extern "C" size_t musc_b200_bank_bytes(long long rows, int channels) {
+  if (rows <= 0 || channels <= 0) return 0;
+  return bank_layout(rows, channels).total;
+}
+
+extern "C" int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
+                                   size_t bank_bytes, musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(rows, channels));
+  if (!z || !bank) return fail(MUSC_B200_ERR_INVALID, "prep_bank: null pointer");
+  if (reinterpret_cast<uintptr_t>(z) % 16 != 0 || reinterpret_cast<uintptr_t>(bank) % 1024 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "prep_bank: z must be 16-byte and bank 1024-byte aligned");
+  const BankLayout l = bank_layout(rows, channels);
+  if (bank_bytes < l.total) return fail(MUSC_B200_ERR_WORKSPACE, "prep_bank: bank smaller than musc_b200_bank_bytes");
+  MUSC_TRY(require_sm100());
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* b = static_cast<uint8_t*>(bank);
+  const long long blocks = (rows + kPrepWarps - 1) / kPrepWarps;
+  prep_bank_kernel<<<(unsigned)blocks, kPrepWarps * 32, 0, s>>>(
+      z, rows, channels, reinterpret_cast<__half*>(b + l.hi), reinterpret_cast<__half*>(b + l.lo),
+      reinterpret_cast<float*>(b + l.norm), reinterpret_cast<float*>(b + l.inv));
+  return check_launch("prep_bank_kernel");
+}
+
+extern "C" int musc_b200_nearest(const void* query_bank, long long query_rows, long long query_first_row,
+                                 const void* ref_bank, long long ref_rows, int channels,
+                                 int patches_per_image, float* nearest_sq, musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(query_rows, channels));
+  MUSC_TRY(check_bank_args(ref_rows, channels));
+  if (!query_bank || !ref_bank || !nearest_sq) return fail(MUSC_B200_ERR_INVALID, "nearest: null pointer");
+  if (reinterpret_cast<uintptr_t>(query_bank) % 1024 != 0 || reinterpret_cast<uintptr_t>(ref_bank) % 1024 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest: banks must be 1024-byte aligned");
+  if (patches_per_image <= 0 || ref_rows % patches_per_image != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest: ref_rows must be a multiple of patches_per_image");
+  if (query_first_row < 0 || query_first_row + query_rows > ref_rows)
+    return fail(MUSC_B200_ERR_INVALID, "nearest: query rows must lie inside the reference pool");
+  if (reinterpret_cast<uintptr_t>(nearest_sq) % 4 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest: output must be 4-byte aligned");
+  MUSC_TRY(require_sm100());
+  return nearest_launch(query_bank, query_rows, query_first_row, ref_bank, ref_rows, channels,
+                        patches_per_image, nearest_sq, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
+                                      int rank_lo, int rank_hi, double* scores, musc_b200_stream stream) {
+  if (!nearest_sq || !scores) return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: null pointer");
+  if (query_rows <= 0 || n_images < 2)
+    return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: requires rows > 0 and N >= 2");
+  if (!(0 <= rank_lo && rank_lo < rank_hi && rank_hi <= n_images - 1))
+    return fail(MUSC_B200_ERR_INVALID, "Require valid nonempty trimmed ranks 0<=a<b<=N-1.");
+  if (query_rows > 0x7FFFFFFFLL * 32) return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: too many rows");
+  MUSC_TRY(require_sm100());
+  return trimmed_launch(nearest_sq, query_rows, n_images, rank_lo, rank_hi, scores,
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t musc_b200_msm_workspace_bytes(int n, int p, int c) {
+  if (n <= 0 || p <= 0 || c <= 0) return 0;
+  const long long rows = (long long)n * p;
+  return bank_layout(rows, c).total + align_up((size_t)rows * n * 4, 1024);
+}
+
+extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi, double* scores,
+                             void* workspace, size_t workspace_bytes, musc_b200_stream stream) {
+  if (!z || !scores || !workspace) return fail(MUSC_B200_ERR_INVALID, "msm: null pointer");
+  if (!(n >= 2 && p > 0 && c > 0)) return fail(MUSC_B200_ERR_INVALID, "Requires N>=2, P>0, C>0.");
+  if (!(0 <= rank_lo && rank_lo < rank_hi && rank_hi <= n - 1))
+    return fail(MUSC_B200_ERR_INVALID, "Require valid nonempty trimmed ranks 0<=a<b<=N-1.");
+  const long long rows = (long long)n * p;
+  MUSC_TRY(check_bank_args(rows, c));
+  if (workspace_bytes < musc_b200_msm_workspace_bytes(n, p, c))
+    return fail(MUSC_B200_ERR_WORKSPACE, "msm: workspace smaller than musc_b200_msm_workspace_bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) % 1024 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "msm: workspace must be 1024-byte aligned");
+  const size_t bank_size = bank_layout(rows, c).total;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* table = reinterpret_cast<float*>(ws + bank_size);
+  MUSC_TRY(musc_b200_prep_bank(z, rows, c, ws, bank_size, stream));
+  MUSC_TRY(musc_b200_nearest(ws, rows, 0, ws, rows, c, p, table, stream));
+  return musc_b200_trimmed_mean(table, rows, n, rank_lo, rank_hi, scores, stream);
+}

@@ -1,0 +1,100 @@
+// Status/error plumbing, device checks and the device-side error word.
+#include "common.cuh"
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+// Written by kernels whose bounded waits expired; read by the host.
+__device__ int musc_device_error = 0;
+
+namespace musc {
+
+static thread_local std::string g_last_error;
+
+int fail(int status, const std::string& message) {
+  g_last_error = message;
+  return status;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  std::string msg = std::string(what) + ": " + cudaGetErrorName(err) + " (" +
+                    cudaGetErrorString(err) + ")";
+  return fail(MUSC_B200_ERR_CUDA, msg);
+}
+
+namespace {
+struct DeviceInfo {
+  int major = -1, minor = -1, sms = 0, smem_optin = 0;
+};
+std::mutex g_info_mutex;
+std::vector<DeviceInfo> g_info;
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  MUSC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_info_mutex);
+  if ((int)g_info.size() <= dev) g_info.resize(dev + 1);
+  DeviceInfo& d = g_info[dev];
+  if (d.major < 0) {
+    MUSC_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+    MUSC_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+    MUSC_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    MUSC_CUDA(cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  }
+  *out = d;
+  return MUSC_B200_OK;
+}
+}  // namespace
+
+int require_sm100(void) {
+  DeviceInfo d;
+  MUSC_TRY(device_info(&d));
+  if (d.major != 10 || d.minor != 0)
+    return fail(MUSC_B200_ERR_DEVICE, "musc_b200 kernels are built for sm_100a; current device is sm_" +
+                                          std::to_string(d.major) + std::to_string(d.minor));
+  return MUSC_B200_OK;
+}
+
+int sm_count(void) {
+  DeviceInfo d;
+  if (device_info(&d) != MUSC_B200_OK) return 0;
+  return d.sms;
+}
+
+int smem_optin(void) {
+  DeviceInfo d;
+  if (device_info(&d) != MUSC_B200_OK) return 0;
+  return d.smem_optin;
+}
+
+int* device_error_ptr(void) {
+  static std::mutex m;
+  static std::vector<int*> ptrs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(m);
+  if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, musc_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+}  // namespace musc
+
+extern "C" int musc_b200_abi_version(void) { return 1; }
+
+extern "C" const char* musc_b200_last_error(void) { return musc::g_last_error.c_str(); }
+
+extern "C" int musc_b200_take_device_error(int* code) {
+  if (!code) return musc::fail(MUSC_B200_ERR_INVALID, "take_device_error: null output pointer");
+  MUSC_CUDA(cudaDeviceSynchronize());
+  int value = 0, zero = 0;
+  MUSC_CUDA(cudaMemcpyFromSymbol(&value, musc_device_error, sizeof(int)));
+  MUSC_CUDA(cudaMemcpyToSymbol(musc_device_error, &zero, sizeof(int)));
+  *code = value;
+  return MUSC_B200_OK;
+}

@@ -1,0 +1,229 @@
+"""Torch-facing wrappers of the C-ABI entry points.
+
+Every function takes and returns CUDA tensors, allocates its outputs and
+workspaces with torch's caching allocator, and enqueues the kernels on torch's
+current stream of the input's device (the reference launches on the same
+stream, ``models/modules/_cuda_runtime.py:95-100``).  Nothing here computes on
+the CPU: a missing library or a non-sm_100 device raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def _aligned_empty(nbytes: int, device: torch.device, align: int = 1024) -> torch.Tensor:
+    """A uint8 buffer whose data pointer is ``align``-byte aligned."""
+    raw = torch.empty(nbytes + align, dtype=torch.uint8, device=device)
+    off = (-raw.data_ptr()) % align
+    return raw[off:off + nbytes]
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f'{what}: expected a CUDA tensor (the b200 backend has no CPU path)')
+
+
+# --------------------------------------------------------------------------- LNAMD
+def lnamd(tokens: torch.Tensor, radii: Sequence[int] = (1, 3, 5), l2_normalize: bool = True,
+          out: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
+    """LNAMD of one layer's tokens ``(B, 1+P, C)`` -> one ``(B, P, C)`` fp32 tensor per radius.
+
+    LayerNorm over the whole ``(C, side, side)`` image, zero-padded r x r mean
+    (``models/modules/_encoder_gpu.py:33-37``) and, if ``l2_normalize``, the
+    per-patch L2 normalisation of ``models/musc.py:238``.
+    """
+    _require_cuda(tokens, 'lnamd')
+    if tokens.ndim != 3 or tokens.dtype not in _DTYPES:
+        raise ValueError('lnamd: expected (B, 1+P, C) float32/float16/bfloat16 tokens')
+    tokens = tokens.contiguous()
+    b, length, c = tokens.shape
+    p = length - 1
+    radii = [int(r) for r in radii]
+    if out is None:
+        out = [torch.empty(b, p, c, dtype=torch.float32, device=tokens.device) for _ in radii]
+    outs = list(out)
+    for o in outs:
+        if o.shape != (b, p, c) or o.dtype != torch.float32 or not o.is_contiguous():
+            raise ValueError('lnamd: outputs must be contiguous float32 (B, P, C)')
+    _launch_lnamd(tokens, radii, outs, p * c, c, l2_normalize)
+    return outs
+
+
+def lnamd_layers(tokens: Sequence[torch.Tensor], r: int, l2_normalize: bool = False) -> torch.Tensor:
+    """The reference aggregation layout: ``(B, P, layers, C)`` for one radius.
+
+    Matches ``aggregate_features`` / ``RadiusAggregationCache.__call__``
+    (``models/modules/_encoder_gpu.py:14-42``, ``_aggregation_cache.py:15-58``):
+    the per-layer results stacked on dim 2 (``_LNAMD.py:126``).
+    """
+    first = tokens[0]
+    _require_cuda(first, 'lnamd_layers')
+    b, length, c = first.shape
+    p = length - 1
+    layers = len(tokens)
+    result = torch.empty(b, p, layers, c, dtype=torch.float32, device=first.device)
+    for li, t in enumerate(tokens):
+        if t.shape != first.shape or t.dtype != first.dtype or t.device != first.device:
+            raise ValueError('lnamd_layers: all layers must share shape, dtype and device')
+        view = result[:, :, li, :]
+        _launch_lnamd(t.contiguous(), [r], [view], p * layers * c, layers * c, l2_normalize)
+    return result
+
+
+def _launch_lnamd(tokens: torch.Tensor, radii: list[int], outs: list[torch.Tensor],
+                  image_stride: int, patch_stride: int, l2_normalize: bool) -> None:
+    b, length, c = tokens.shape
+    dev = tokens.device
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        ws_bytes = lib.musc_b200_lnamd_workspace_bytes(b)
+        ws = _aligned_empty(ws_bytes, dev, 256)
+        radii_arr = (ctypes.c_int * len(radii))(*radii)
+        out_arr = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+        st = lib.musc_b200_lnamd(_ptr(tokens), _DTYPES[tokens.dtype], b, length, c, len(radii),
+                                 radii_arr, out_arr, image_stride, patch_stride, int(l2_normalize),
+                                 _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(st, 'musc_b200_lnamd')
+
+
+def lnamd_super_fast(tokens: torch.Tensor, out_side: int = 28, l2_normalize: bool = True,
+                     out: torch.Tensor | None = None, image_stride: int | None = None,
+                     patch_stride: int | None = None) -> torch.Tensor:
+    """r=3 LNAMD then adaptive pooling to ``out_side``^2 patches (``_super_fast.py:17-27``)."""
+    _require_cuda(tokens, 'lnamd_super_fast')
+    if tokens.ndim != 3 or tokens.dtype not in _DTYPES:
+        raise ValueError('lnamd_super_fast: expected (B, 1+P, C) tokens')
+    tokens = tokens.contiguous()
+    b, length, c = tokens.shape
+    q = out_side * out_side
+    if out is None:
+        out = torch.empty(b, q, c, dtype=torch.float32, device=tokens.device)
+        image_stride, patch_stride = q * c, c
+    dev = tokens.device
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        ws_bytes = lib.musc_b200_lnamd_workspace_bytes(b)
+        ws = _aligned_empty(ws_bytes, dev, 256)
+        st = lib.musc_b200_lnamd_super_fast(_ptr(tokens), _DTYPES[tokens.dtype], b, length, c, out_side,
+                                            _ptr(out), image_stride, patch_stride, int(l2_normalize),
+                                            _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(st, 'musc_b200_lnamd_super_fast')
+    return out
+
+
+# --------------------------------------------------------------------------- MSM
+def trimmed_ranks(n_images: int, topmin_min: float = 0, topmin_max: float = 0.3) -> tuple[int, int]:
+    """``[a, b)`` as the reference derives them (``_MSM_gpu.py:706-709``; ``_MSM.py:20-28``)."""
+    a = int((n_images - 1) * topmin_min) if topmin_min < 1 else int(topmin_min)
+    b = int((n_images - 1) * topmin_max) if topmin_max < 1 else int(topmin_max)
+    a, b = sorted((a, b))
+    if not 0 <= a < b <= n_images - 1:
+        raise ValueError('Require valid nonempty trimmed ranks 0<=a<b<=N-1.')
+    return a, b
+
+
+def prep_bank(z: torch.Tensor) -> torch.Tensor:
+    """Split-fp16 tensor-core operand bank of ``z`` ``(rows, C)`` fp32."""
+    _require_cuda(z, 'prep_bank')
+    if z.ndim != 2 or z.dtype != torch.float32:
+        raise ValueError('prep_bank: expected (rows, C) float32')
+    z = z.contiguous()
+    rows, c = z.shape
+    dev = z.device
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        nbytes = lib.musc_b200_bank_bytes(rows, c)
+        bank = _aligned_empty(nbytes, dev)
+        _lib.check(lib.musc_b200_prep_bank(_ptr(z), rows, c, _ptr(bank), nbytes, _stream(dev)),
+                   'musc_b200_prep_bank')
+    return bank
+
+
+def nearest(query_bank: torch.Tensor, query_rows: int, query_first_row: int, ref_bank: torch.Tensor,
+            ref_rows: int, channels: int, patches: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Squared nearest-patch minima ``(n_images, query_rows)`` fp32 (self image = FLT_MAX)."""
+    dev = query_bank.device
+    n_images = ref_rows // patches
+    if out is None:
+        out = torch.empty(n_images, query_rows, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_nearest(_ptr(query_bank), query_rows, query_first_row, _ptr(ref_bank),
+                                          ref_rows, channels, patches, _ptr(out), _stream(dev))
+        _lib.check(st, 'musc_b200_nearest')
+    return out
+
+
+def trimmed_mean(nearest_sq: torch.Tensor, rank_lo: int, rank_hi: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Interval average of ``sqrt(nearest_sq)`` over images -> ``(query_rows,)`` float64."""
+    n_images, rows = nearest_sq.shape
+    dev = nearest_sq.device
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float64, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_trimmed_mean(_ptr(nearest_sq), rows, n_images, rank_lo, rank_hi,
+                                               _ptr(out), _stream(dev))
+        _lib.check(st, 'musc_b200_trimmed_mean')
+    return out
+
+
+def msm(Z: torch.Tensor, topmin_min: float = 0, topmin_max: float = 0.3) -> torch.Tensor:
+    """Mutual scoring of one bank ``(N, P, C)`` fp32 -> ``(N, P)`` float64 (``_MSM.py:53-59``)."""
+    if Z.ndim != 3 or not Z.is_cuda or Z.dtype != torch.float32:
+        raise ValueError('Expected CUDA FP32 features with shape (N,P,C).')
+    n, p, c = Z.shape
+    if not (n >= 2 and p > 0 and c > 0):
+        raise ValueError('Requires N>=2, P>0, C>0.')
+    a, b = trimmed_ranks(n, topmin_min, topmin_max)
+    dev = Z.device
+    z = Z.contiguous()
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        ws_bytes = lib.musc_b200_msm_workspace_bytes(n, p, c)
+        ws = _aligned_empty(ws_bytes, dev)
+        scores = torch.empty(n, p, dtype=torch.float64, device=dev)
+        st = lib.musc_b200_msm(_ptr(z), n, p, c, a, b, _ptr(scores), _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(st, 'musc_b200_msm')
+    return scores
+
+
+# --------------------------------------------------------------------------- reduction
+def score_maps(scores: torch.Tensor, image_size: int = 518, upsampled: bool = False):
+    """``(R, L, N, P)`` float64 scores -> ``(maps (N, s, s), image_max (N,), up or None)``.
+
+    ``models/musc.py:259-288``: layer mean, radius mean, bilinear
+    align_corners=True up-sampling to ``image_size`` and the per-image max.
+    """
+    _require_cuda(scores, 'score_maps')
+    if scores.ndim != 4 or scores.dtype != torch.float64:
+        raise ValueError('score_maps: expected (R, L, N, P) float64')
+    scores = scores.contiguous()
+    r, l, n, p = scores.shape
+    side = math.isqrt(p)
+    if side * side != p:
+        raise ValueError('score_maps: P must be a square')
+    dev = scores.device
+    maps = torch.empty(n, side, side, dtype=torch.float64, device=dev)
+    image_max = torch.empty(n, dtype=torch.float64, device=dev)
+    up = torch.empty(n, image_size, image_size, dtype=torch.float64, device=dev) if upsampled else None
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_score_maps(_ptr(scores), r, l, n, side, image_size, _ptr(maps),
+                                             _ptr(image_max), _ptr(up), _stream(dev))
+        _lib.check(st, 'musc_b200_score_maps')
+    return maps, image_max, up

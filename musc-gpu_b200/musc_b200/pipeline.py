@@ -1,0 +1,158 @@
+"""Device-resident pool scoring: LNAMD -> MSM -> score reduction, 1..G GPUs.
+
+This is the scoring half of ``MuSc.make_category_data``
+(``models/musc.py:224-288``) with every stage on the B200:
+
+* per layer, one LNAMD launch produces the L2-normalised banks of all radii
+  (``models/musc.py:227-245``; the bank assembly ``Z = cat(Z_layers[l])`` of
+  ``:252`` is the output layout itself);
+* per (radius, layer) bank, MSM (``:248-262``) = bank prep, the fused
+  distance/min GEMM and the interval average;
+* layer and radius means, up-sampling and image maxima (``:259-288``).
+
+Multi-GPU (one process per GPU): rank r owns the query images
+``[r*ceil(N/G), ...)``, aggregates only those, all-gathers each bank over NCCL
+(overlapped with the previous bank's GEMM) and scores its query rows against
+the whole pool; self exclusion uses global image indices.  The reference is
+single-device; the sharding is this library's addition.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from . import ops
+
+
+def shard_range(n_images: int, world: int, rank: int) -> tuple[int, int, int]:
+    """``(first, end, per)``: rank's query images ``[first, end)``, ``per = ceil(N/G)``.
+
+    Ranks take ``per`` images each in order, so the gathered, per-padded banks
+    hold the pool contiguously in their first ``N`` images.
+    """
+    if n_images <= 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError('shard_range: requires N > 0, world > 0, 0 <= rank < world')
+    per = -(-n_images // world)
+    first = min(n_images, rank * per)
+    end = min(n_images, first + per)
+    return first, end, per
+
+
+@dataclass
+class PoolScores:
+    scores: torch.Tensor      # (R, L, n_local, P) float64, this rank's query images
+    maps: torch.Tensor        # (n_local, side, side) float64
+    image_max: torch.Tensor   # (n_local,) float64
+    first_image: int
+    n_images: int
+
+
+def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
+               radii: Sequence[int] = (1, 3, 5), topmin_min: float = 0, topmin_max: float = 0.3,
+               image_size: int = 518, super_fast_side: int | None = None,
+               group=None, kernels=ops) -> PoolScores:
+    """Score one pool from device-resident tokens.
+
+    ``tokens``: per hooked layer, this rank's ``(n_local, 1+P, C)`` tokens
+    (all ``N`` images when running on one GPU).  ``super_fast_side``: if set,
+    the super-fast profile (r=3 LNAMD, adaptive pooling to that side).
+    ``group``: a ``torch.distributed`` process group (None = single GPU).
+    ``kernels``: the operator set (``musc_b200.ops``, the CUDA library); the
+    CPU tests of the sharding logic substitute the numpy oracle here.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group) if group is not None else 1
+    rank = dist.get_rank(group) if group is not None else 0
+    first_tok = tokens[0]
+    dev = first_tok.device
+    n_local, length, c = first_tok.shape
+    if n_images is None:
+        n_images = n_local * world if world == 1 else None
+        if n_images is None:
+            raise ValueError('score_pool: n_images is required with a process group')
+    first, end, per = shard_range(n_images, world, rank)
+    if end - first != n_local:
+        raise ValueError(f'score_pool: rank {rank} holds {n_local} images, expected {end - first}')
+    a, b = kernels.trimmed_ranks(n_images, topmin_min, topmin_max)
+    if super_fast_side is not None:
+        radii = (3,)
+        p = super_fast_side * super_fast_side
+    else:
+        p = length - 1
+    side = math.isqrt(p)
+    n_r, n_l = len(radii), len(tokens)
+
+    # 1. LNAMD of the local images into (R*L) local banks, padded to `per` images.
+    local = torch.zeros(n_l, n_r, per, p, c, dtype=torch.float32, device=dev)
+    for li, t in enumerate(tokens):
+        if n_local == 0:
+            continue
+        if super_fast_side is not None:
+            kernels.lnamd_super_fast(t, super_fast_side, True, out=local[li, 0, :n_local],
+                                 image_stride=p * c, patch_stride=c)
+        else:
+            kernels.lnamd(t, radii, True, out=[local[li, ri, :n_local] for ri in range(n_r)])
+
+    # 2. Per bank: (gather), prep, nearest, interval average.
+    banks = [(li, ri) for ri in range(n_r) for li in range(n_l)]
+    scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
+    rows = n_images * p
+    q_rows = n_local * p
+    nearest_buf = torch.empty(n_images, max(q_rows, 1), dtype=torch.float32, device=dev)
+    if world > 1:
+        full = [torch.empty(world * per, p, c, dtype=torch.float32, device=dev) for _ in range(2)]
+        works = [None] * len(banks)
+        works[0] = dist.all_gather_into_tensor(full[0], local[banks[0]], group=group, async_op=True)
+    for k, (li, ri) in enumerate(banks):
+        if world > 1:
+            if k + 1 < len(banks):
+                nxt = banks[k + 1]
+                works[k + 1] = dist.all_gather_into_tensor(full[(k + 1) % 2], local[nxt], group=group,
+                                                           async_op=True)
+            works[k].wait()
+            z_full = full[k % 2][:n_images]
+        else:
+            z_full = local[li, ri, :n_images]
+        bank = kernels.prep_bank(z_full.reshape(rows, c))
+        if q_rows == 0:
+            continue
+        if world > 1:
+            qbank = kernels.prep_bank(local[li, ri, :n_local].reshape(q_rows, c))
+        else:
+            qbank = bank
+        near = kernels.nearest(qbank, q_rows, first * p, bank, rows, c, p, out=nearest_buf)
+        kernels.trimmed_mean(near, a, b, out=scores[ri, li].view(-1))
+
+    # 3. Layer/radius means, up-sampling, image maxima for the local images.
+    if n_local:
+        maps, image_max, _ = kernels.score_maps(scores, image_size)
+    else:
+        maps = torch.empty(0, side, side, dtype=torch.float64, device=dev)
+        image_max = torch.empty(0, dtype=torch.float64, device=dev)
+    return PoolScores(scores, maps, image_max, first, n_images)
+
+
+def gather_pool(result: PoolScores, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """All ranks' ``maps`` and ``image_max`` concatenated in image order (every rank gets them)."""
+    import torch.distributed as dist
+
+    if group is None:
+        return result.maps, result.image_max
+    world = dist.get_world_size(group)
+    _, _, per = shard_range(result.n_images, world, 0)
+    side = result.maps.shape[-1] if result.maps.ndim == 3 else 0
+    dev = result.image_max.device
+    n_local = result.image_max.shape[0]
+    maps = torch.zeros(per, side, side, dtype=torch.float64, device=dev)
+    mx = torch.zeros(per, dtype=torch.float64, device=dev)
+    maps[:n_local] = result.maps
+    mx[:n_local] = result.image_max
+    all_maps = torch.empty(world * per, side, side, dtype=torch.float64, device=dev)
+    all_mx = torch.empty(world * per, dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(all_maps, maps, group=group)
+    dist.all_gather_into_tensor(all_mx, mx, group=group)
+    return all_maps[:result.n_images], all_mx[:result.n_images]

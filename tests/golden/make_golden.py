@@ -1,0 +1,155 @@
+"""Generate the golden fixtures by running the reference's own CPU code.
+
+Run from the repository root in a container where the reference checkout is
+available (it is read only through ``--reference``)::
+
+    python tests/golden/make_golden.py --reference <path to the MuSc checkout>
+
+The script imports the reference's ``original`` modules --
+``models/modules/_MSM.py`` (``MSM``), ``models/modules/_LNAMD.py``
+(``LNAMD._embed``), ``models/modules/_encoder_gpu.py``
+(``aggregate_features``) and ``models/modules/_super_fast.py``
+(``SuperFastAggregation``) -- and evaluates the score reduction of
+``models/musc.py:259-288`` with the same torch calls.  Inputs are either stored
+in the fixture (small cases) or regenerated from ``musc_b200.synthetic`` with
+the recorded seed (the N=16 prototype-mixture pool).  Nothing at test time reads
+the reference; the tests read only the ``.npz`` files written here.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path.insert(0, str(REPO / 'musc-gpu_b200'))
+
+
+def _reference_modules(reference: str):
+    sys.path.insert(0, reference)
+    from models.modules._MSM import MSM  # noqa: E402
+    from models.modules._LNAMD import LNAMD  # noqa: E402
+    from models.modules import _encoder_gpu, _super_fast  # noqa: E402
+    return MSM, LNAMD, _encoder_gpu, _super_fast
+
+
+def _unit_rows(x: torch.Tensor) -> torch.Tensor:
+    return x / x.norm(dim=-1, keepdim=True)
+
+
+def make_msm_small(MSM) -> dict:
+    """Small MSM cases with stored inputs, including the edge cases."""
+    g = torch.Generator().manual_seed(1234)
+    out = {}
+    # (name, n, p, c, topmin_min, topmin_max)
+    cases = [('a', 5, 49, 64, 0, 0.3), ('b', 9, 49, 64, 0, 0.3),
+             ('c', 16, 49, 64, 0.1, 0.5), ('d', 12, 64, 32, 0, 0.3),
+             ('e', 7, 100, 128, 0, 0.9)]
+    for name, n, p, c, lo, hi in cases:
+        z = _unit_rows(torch.randn(n, p, c, generator=g))
+        if name == 'b':
+            # duplicated patches (distance 0) and exact ties across images
+            z[3, :10] = z[0, :10]
+            z[5, 20:30] = z[0, 20:30]
+            z[6] = z[2]
+        if name == 'd':
+            # constant image: all its patches identical
+            z[4] = z[4, :1].expand(p, c)
+        s = MSM(z, 'cpu', topmin_min=lo, topmin_max=hi)
+        out[f'{name}_z'] = z.numpy()
+        out[f'{name}_scores'] = s.numpy()
+        out[f'{name}_ranks'] = np.array([lo, hi], dtype=np.float64)
+    return out
+
+
+def make_lnamd_small(LNAMD, encoder_gpu, super_fast) -> dict:
+    """LNAMD (r=1/3/5), the direct-pool form and the super-fast pooling on small C."""
+    g = torch.Generator().manual_seed(99)
+    b, c = 3, 32
+    layers = [torch.randn(b, 1370, c, generator=g) * 2.0 + 0.5 for _ in range(2)]
+    out = {'tokens': torch.stack(layers).numpy()}
+    for r in (1, 3, 5):
+        lnamd = LNAMD(device='cpu', r=r, feature_dim=c, feature_layer=[1, 2])
+        emb = lnamd._embed(layers, return_cpu=True)
+        direct = encoder_gpu.aggregate_features(lnamd, layers, return_cpu=True)
+        out[f'embed_r{r}'] = emb.numpy()
+        out[f'direct_r{r}'] = direct.numpy()
+    # super-fast profile: one layer, r = 3, 37x37 -> 28x28
+    lnamd3 = LNAMD(device='cpu', r=3, feature_dim=c, feature_layer=[1])
+    agg = super_fast.SuperFastAggregation()
+    sf = agg(lnamd3, [layers[0]], return_cpu=True)
+    out['superfast'] = sf.numpy()
+    return out
+
+
+def _reduce_like_musc(scores: torch.Tensor, image_size: int):
+    """``models/musc.py:259-288`` on a ``(R, L, N, P)`` float64 tensor."""
+    per_r = torch.stack([torch.mean(scores[r], 0) for r in range(scores.shape[0])])
+    maps = torch.mean(per_r, 0)
+    n, p = maps.shape
+    h = int(np.sqrt(p))
+    up = F.interpolate(maps.view(n, 1, h, h), size=image_size, mode='bilinear', align_corners=True)
+    up = up.cpu().numpy()
+    return maps.view(n, h, h).numpy(), up.reshape(n, -1).max(-1), up
+
+
+def make_reduce_small() -> dict:
+    g = torch.Generator().manual_seed(7)
+    scores = torch.rand(3, 4, 5, 1369, generator=g, dtype=torch.float64) + 1.0
+    maps, image_max, up = _reduce_like_musc(scores, 518)
+    return {'scores': scores.numpy(), 'maps': maps, 'image_max': image_max,
+            'up_rows_0_7_517': up[:, 0, [0, 7, 517], :]}
+
+
+def make_pool16(MSM, LNAMD, encoder_gpu) -> dict:
+    """Config 1: N=16 prototype-mixture pool, 4 layers x r{1,3,5}, full reference pipeline."""
+    from musc_b200.synthetic import prototype_mixture
+    n, seed = 16, 0
+    tokens = prototype_mixture(n, n_layers=4, c=1024, side=37, seed=seed)
+    radii = (1, 3, 5)
+    scores = torch.empty(len(radii), 4, n, 1369, dtype=torch.float64)
+    probe_rows = np.arange(0, n * 1369, 977)
+    bank_probe = np.empty((len(radii), 4, len(probe_rows), 1024), dtype=np.float32)
+    torch.set_num_threads(os.cpu_count() or 1)
+    for ri, r in enumerate(radii):
+        lnamd = LNAMD(device='cpu', r=r, feature_dim=1024, feature_layer=[1, 2, 3, 4])
+        feats = lnamd._embed(tokens, return_cpu=True)
+        feats /= feats.norm(dim=-1, keepdim=True)
+        for li in range(4):
+            z = feats[:, :, li, :].contiguous()
+            bank_probe[ri, li] = z.reshape(-1, 1024)[probe_rows].numpy()
+            scores[ri, li] = MSM(z, 'cpu', topmin_min=0, topmin_max=0.3)
+    maps, image_max, _ = _reduce_like_musc(scores, 518)
+    return {'seed': np.array(seed), 'n': np.array(n), 'scores': scores.numpy(),
+            'maps': maps, 'image_max': image_max, 'probe_rows': probe_rows,
+            'bank_probe': bank_probe}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--reference', required=True)
+    ap.add_argument('--only', default='')
+    args = ap.parse_args()
+    MSM, LNAMD, encoder_gpu, super_fast = _reference_modules(args.reference)
+    torch.manual_seed(0)
+    jobs = {'msm_small': lambda: make_msm_small(MSM),
+            'lnamd_small': lambda: make_lnamd_small(LNAMD, encoder_gpu, super_fast),
+            'reduce_small': make_reduce_small,
+            'pool16': lambda: make_pool16(MSM, LNAMD, encoder_gpu)}
+    for name, job in jobs.items():
+        if args.only and name not in args.only.split(','):
+            continue
+        data = job()
+        np.savez_compressed(HERE / f'{name}.npz', **data)
+        print(name, {k: v.shape for k, v in data.items()})
+
+
+if __name__ == '__main__':
+    main()

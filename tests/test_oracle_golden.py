@@ -1,0 +1,85 @@
+"""Pin the numpy oracle against golden vectors produced by the reference itself.
+
+The fixtures under tests/golden were written by tests/golden/make_golden.py,
+which runs the reference's ``original`` modules (``_MSM.MSM``,
+``LNAMD._embed``, ``aggregate_features``, ``SuperFastAggregation``) and the
+score reduction of ``models/musc.py:259-288``.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from oracle import lnamd as olnamd
+from oracle import msm as omsm
+from oracle import reduce as oreduce
+
+
+@pytest.mark.parametrize('case', ['a', 'b', 'c', 'd', 'e'])
+def test_msm_small_cases(case):
+    g = golden('msm_small')
+    z, want = g[f'{case}_z'], g[f'{case}_scores']
+    lo, hi = g[f'{case}_ranks']
+    got = omsm.msm(z, lo, hi)
+    assert got.dtype == np.float64 and got.shape == want.shape
+    # Exact duplicates put sqrt(fp32 rounding noise) into both sides, so d ~ 0
+    # pairs differ at ~1e-3 absolute; everything else agrees to fp32 rounding.
+    np.testing.assert_allclose(got, want, rtol=2e-5, atol=2e-3 if case in ('b', 'd') else 1e-6)
+
+
+def test_trimmed_ranks_follow_reference():
+    # _MSM.py:20-28 for the configs' pool sizes
+    assert omsm.trimmed_ranks(16) == (0, 4)
+    assert omsm.trimmed_ranks(100) == (0, 29)
+    assert omsm.trimmed_ranks(200) == (0, 59)
+    assert omsm.trimmed_ranks(1024) == (0, 306)
+    assert omsm.trimmed_ranks(16, 0.1, 0.5) == (1, 7)
+
+
+@pytest.mark.parametrize('r', [1, 3, 5])
+def test_lnamd_matches_embed_and_direct_pool(r):
+    g = golden('lnamd_small')
+    tokens = g['tokens']                      # (layers, B, 1370, C)
+    embed, direct = g[f'embed_r{r}'], g[f'direct_r{r}']   # (B, P, layers, C)
+    np.testing.assert_allclose(embed, direct, rtol=0, atol=2e-5)
+    for li in range(tokens.shape[0]):
+        got = olnamd.lnamd(tokens[li], r)
+        np.testing.assert_allclose(got, embed[:, :, li, :], rtol=1e-5, atol=2e-5)
+
+
+def test_super_fast_pooling():
+    g = golden('lnamd_small')
+    got = olnamd.lnamd_super_fast(g['tokens'][0], 28)
+    np.testing.assert_allclose(got, g['superfast'][:, :, 0, :], rtol=1e-5, atol=2e-5)
+
+
+def test_score_reduction():
+    g = golden('reduce_small')
+    maps, image_max = oreduce.image_scores(g['scores'], 518)
+    np.testing.assert_allclose(maps, g['maps'], rtol=0, atol=1e-14)
+    np.testing.assert_allclose(image_max, g['image_max'], rtol=0, atol=1e-14)
+    up = oreduce.bilinear_align_corners(maps, 518)
+    np.testing.assert_allclose(up[:, [0, 7, 517], :], g['up_rows_0_7_517'], rtol=0, atol=1e-14)
+
+
+def test_pool16_banks_and_one_bank_scores():
+    """Config 1: the regenerated tokens reproduce the reference's banks and scores."""
+    import torch
+    from musc_b200.synthetic import prototype_mixture
+    g = golden('pool16')
+    n = int(g['n'])
+    tokens = prototype_mixture(n, n_layers=4, c=1024, side=37, seed=int(g['seed']))
+    rows = g['probe_rows']
+    for ri, r in enumerate((1, 3, 5)):
+        for li in (0, 3):
+            z = olnamd.bank(tokens[li].numpy(), r)
+            np.testing.assert_allclose(z.reshape(-1, 1024)[rows], g['bank_probe'][ri, li],
+                                       rtol=1e-4, atol=2e-6)
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    z = olnamd.bank(tokens[2].numpy(), 3)
+    got = omsm.msm(z)
+    np.testing.assert_allclose(got, g['scores'][1, 2], rtol=2e-5, atol=0)
+    maps, image_max = oreduce.image_scores(g['scores'], 518)
+    np.testing.assert_allclose(maps, g['maps'], rtol=0, atol=1e-14)
+    np.testing.assert_allclose(image_max, g['image_max'], rtol=0, atol=1e-14)
