@@ -18,8 +18,10 @@ average) and the score reduction (maps, up-sampled image maxima).
   the host cores, on a bounded sample, scaled to images/s.
 
 ``--gpus N`` under torchrun: rank r scores query images [r*ceil(N/G), ...)
-against the whole pool (banks all-gathered over NCCL); the time is the max
-over ranks and ``value`` counts the whole pool (strong scaling).
+against the whole pool: banks are all-gathered over NCCL, each rank evaluates a
+balanced share of the symmetric distance tiles and a MIN reduce-scatter hands
+each rank its query rows' minima; the time is the max over ranks and ``value``
+counts the whole pool (strong scaling).
 ``--impl reference`` times the CPU oracle port of the reference path instead.
 """
 from __future__ import annotations
@@ -46,7 +48,6 @@ C = 1024
 P = SIDE * SIDE
 METRIC = 'pool images scored/sec (1369x1024 patches, 4 layers x 3 radii)'
 UNIT = 'images/s'
-MSM_FLOP_PER_BANK = 2.0 * C * P * P * N_POOL * (N_POOL - 1)   # directed, SURVEY 8(d)
 
 
 def _args():
@@ -198,6 +199,19 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def symmetric_tiles(rows: int, patches: int, n_images: int, bm: int = 128, bn: int = 256) -> int:
+    """Tiles the symmetric nearest kernel evaluates (tiles holding an img(r) < img(c) element)."""
+    num_m, num_n = -(-rows // bm), -(-rows // bn)
+    total = 0
+    for m in range(num_m):
+        img = m * bm // patches
+        if img >= n_images - 1:
+            continue
+        need = (img + 1) * patches - bn + 1
+        total += num_n - (0 if need <= 0 else -(-need // bn))
+    return total
+
+
 # ----------------------------------------------------------------- GPU arm
 def run_b200(args):
     import torch
@@ -226,7 +240,7 @@ def run_b200(args):
 
     # Instrument the dominant kernel's launches with events on its stream.
     near_events = []
-    orig_nearest = ops.nearest
+    orig_nearest = ops.nearest_pool
 
     def timed_nearest(*a, **k):
         s = torch.cuda.current_stream(dev)
@@ -242,7 +256,7 @@ def run_b200(args):
     kern = Kernels()
     for name in ('lnamd', 'lnamd_super_fast', 'prep_bank', 'trimmed_mean', 'score_maps', 'trimmed_ranks'):
         setattr(kern, name, getattr(ops, name))
-    kern.nearest = timed_nearest
+    kern.nearest_pool = timed_nearest
 
     def step():
         return pipeline.score_pool(tokens, n_images=pool, radii=RADII, group=group, kernels=kern)
@@ -308,14 +322,15 @@ def run_b200(args):
         ms_per_step = elapsed_ms / args.steps
         value = pool / (ms_per_step / 1e3)
         n_local = end - first
-        q_rows = n_local * P
-        achieved_tflops = MSM_FLOP_PER_BANK * (n_local / pool) / (near_avg_ms / 1e3) / 1e12
-        # executed tensor-core work: 3 MMA passes over whole 128 x 256 tiles
-        tiles_m = math.ceil(q_rows / 128)
-        tiles_n = math.ceil(pool * P / 256)
-        mma_tflops = 3 * 2.0 * tiles_m * 128 * tiles_n * 256 * C / (near_avg_ms / 1e3) / 1e12
+        # algorithmic (directed) MSM flops per bank: 2*C*P^2*N*(N-1), this rank's share
+        msm_flop_per_bank = 2.0 * C * P * P * pool * (pool - 1)
+        achieved_tflops = msm_flop_per_bank * (n_local / pool) / (near_avg_ms / 1e3) / 1e12
+        # executed tensor-core work: 3 MMA passes over the symmetric tiles (whole 128 x 256
+        # tiles holding a pair of different images, each pair once), this rank's share
+        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * P, P, pool) * 128 * 256 * C / world
+                      / (near_avg_ms / 1e3) / 1e12)
         peak = peaks.get('bf16_tflops_sustained', peaks.get('bf16_tflops'))
-        launches_per_step = N_LAYERS * 2 + len(RADII) * N_LAYERS * (4 + (1 if world > 1 else 0)) + 1
+        launches_per_step = N_LAYERS * 2 + len(RADII) * N_LAYERS * 4 + 1
         line = {
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
@@ -323,7 +338,7 @@ def run_b200(args):
             'config': {'workload': f'config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 '
                                    'prototype-mixture tokens resident in HBM',
                        'global_batch': pool, 'seq_len': P, 'parallelism': f'query-shard{world}',
-                       'l2': 'inputs larger than L2 (2.24 GB tokens per step); no flush'},
+                       'l2': f'inputs larger than L2 ({h2d * world / 1e9:.2f} GB tokens per step); no flush'},
             'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
                     'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
             'roofline': {'kernel': 'nearest_kernel', 'bound': 'tensor', 'achieved': achieved_tflops,
@@ -331,7 +346,7 @@ def run_b200(args):
                          'traffic': _traffic(),
                          'peak_kind': f'{peak_kind} bf16 sustained (kernel timed inside a long step)',
                          'mma_executed_tflops': mma_tflops, 'mma_frac': mma_tflops / peak,
-                         'mma_kind': 'kind::f16 (fp16 split hi/lo, 3 passes)',
+                         'mma_kind': 'kind::f16 (fp16 split hi/lo, 3 passes, symmetric tiles)',
                          'launch_ms': near_avg_ms},
             'gpu_launches': launches_per_step * args.steps,
             'clocks': clocks.summary(),

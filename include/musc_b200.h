@@ -121,6 +121,25 @@ int musc_b200_nearest(const void* query_bank, long long query_rows, long long qu
                       const void* ref_bank, long long ref_rows, int channels,
                       int patches_per_image, float* nearest_sq, musc_b200_stream stream);
 
+/* Pool form of the above, for a bank scored against itself: every unordered
+ * pair of patches from different images is evaluated once (symmetric tiles:
+ * row minima give one direction, column minima the other; the reference GPU
+ * driver pairs forward/reverse the same way, _MSM_gpu.py:749-767), halving
+ * the tensor-core work.  The tile list is split into n_parts balanced parts
+ * and this call evaluates part `part` (multi-GPU: one part per rank, then an
+ * element-wise MIN reduction of the tables).
+ * Layout: nearest_sq[block][image][r], block = row / rows_per_block,
+ * r = row % rows_per_block, n_images = rows / patches_per_image; the call
+ * first fills the whole table (musc_b200_nearest_pool_bytes) with FLT_MAX.
+ * rows_per_block = rows gives the plain [image][row] table;
+ * rows_per_block = one rank's rows makes each rank's rows contiguous for a
+ * reduce-scatter. */
+size_t musc_b200_nearest_pool_bytes(long long rows, int patches_per_image, long long rows_per_block);
+
+int musc_b200_nearest_pool(const void* bank, long long rows, int channels, int patches_per_image,
+                           int part, int n_parts, long long rows_per_block, float* nearest_sq,
+                           musc_b200_stream stream);
+
 /* Interval average: scores[q] = mean of ranks [rank_lo, rank_hi) of
  * sqrt(nearest_sq[:, q]) over the n_images - 1 other images, in float32,
  * stored as float64 (_MSM.py:19-30).  0 <= rank_lo < rank_hi <= n_images-1. */

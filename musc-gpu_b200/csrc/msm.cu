@@ -25,8 +25,10 @@
 #include "common.cuh"
 #include "tc.cuh"
 
+#include <algorithm>
 #include <cfloat>
 #include <mutex>
+#include <vector>
 
 namespace musc {
 
@@ -106,9 +108,10 @@ constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr int GROUP_M = 16;  // m-tiles swept together over the reference columns (L2 reuse)
+constexpr int GROUP_M = 64;  // m-tiles swept together over the reference columns (L2 reuse)
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;  // 4 s per wait
 constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, /*fp16*/ 0);
+constexpr float INF = FLT_MAX;
 
 struct Smem {
   uint8_t tiles[STAGES][STAGE_BYTES];  // 1024-aligned base
@@ -129,21 +132,35 @@ struct Params {
   const float* q_inv;
   const float* r_norm;
   const float* r_inv;
-  unsigned int* nearest;  // [n_images][q_rows] float bits
+  unsigned int* nearest;  // float bits, layout [row / rpb][image][row % rpb]
   int* err;
   long long q_rows, r_rows, q_first_row;
-  int patches;  // P
+  long long tile_begin, tile_end;  // linear tile range processed by this launch
+  long long rows_per_block;        // rpb of the nearest layout
+  int blocked;                     // 0: rows_per_block covers every row addressed
+  int patches;                     // P
+  int n_images;
   int num_kb;
   int num_m, num_n;
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int* m_blk, int* n_blk) {
-  const int group = tile / (GROUP_M * num_n);
-  const int first_m = group * GROUP_M;
-  const int gm = min(GROUP_M, num_m - first_m);
-  const int local = tile - group * GROUP_M * num_n;
-  *m_blk = first_m + local % gm;
-  *n_blk = local / gm;
+__host__ __device__ inline void tile_coords(long long tile, int num_m, int num_n, int* m_blk, int* n_blk) {
+  const long long group = tile / ((long long)GROUP_M * num_n);
+  const int first_m = (int)(group * GROUP_M);
+  const int gm = num_m - first_m < GROUP_M ? num_m - first_m : GROUP_M;
+  const long long local = tile - group * GROUP_M * (long long)num_n;
+  *m_blk = first_m + (int)(local % gm);
+  *n_blk = (int)(local / gm);
+}
+
+// Symmetric mode: tile (m, n) holds an element (r, c) with img(r) < img(c).
+__host__ __device__ inline bool sym_needed(int m, int n, long long rows, int patches, int n_images) {
+  const long long r0 = (long long)m * BM;
+  const long long img_r = r0 / patches;
+  if (img_r >= n_images - 1) return false;
+  long long c_last = (long long)n * BN + BN - 1;
+  if (c_last > rows - 1) c_last = rows - 1;
+  return c_last / patches > img_r;
 }
 
 // Bounded wait: true when the phase completed; false after the time limit
@@ -186,14 +203,37 @@ __device__ __forceinline__ bool named_sync_epi_any(int flag) {
   return res != 0;
 }
 
-__device__ __forceinline__ void flush_min(const Params& p, bool row_ok, long long row, int q_img,
-                                          int img, float m) {
-  if (row_ok && img != q_img) {
+__device__ __forceinline__ long long table_index(const Params& p, int img, long long row) {
+  if (!p.blocked) return (long long)img * p.rows_per_block + row;
+  const long long blk = row / p.rows_per_block;
+  return (blk * p.n_images + img) * p.rows_per_block + (row - blk * p.rows_per_block);
+}
+
+__device__ __forceinline__ void flush_min(const Params& p, long long row, int img, float m) {
+  if (m < INF) {
     const float v = m > 0.f ? m : 0.f;
-    atomicMin(p.nearest + (long long)img * p.q_rows + row, __float_as_uint(v));
+    atomicMin(p.nearest + table_index(p, img, row), __float_as_uint(v));
   }
 }
 
+// After the call lane l holds min over the warp's 32 lanes of v[l] (a
+// transposing butterfly: 31 shuffles for 32 columns).
+__device__ __forceinline__ float warp_column_min(float (&v)[32], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = upper ? v[i] : v[i + s];
+      const float keep = upper ? v[i + s] : v[i];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+      v[i] = fminf(keep, recv);
+    }
+  }
+  return v[0];
+}
+
+template <bool SYM>
 __global__ void __launch_bounds__(THREADS, 1)
 nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_constant__ CUtensorMap map_q_lo,
                const __grid_constant__ CUtensorMap map_r_hi, const __grid_constant__ CUtensorMap map_r_lo,
@@ -202,7 +242,6 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.num_m * p.num_n;
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
@@ -240,9 +279,10 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end && ok; tile += gridDim.x) {
         int m_blk, n_blk;
         tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+        if (SYM && !sym_needed(m_blk, n_blk, p.r_rows, p.patches, p.n_images)) continue;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!wait_bounded(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err)) {
             ok = false;
@@ -280,7 +320,12 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end && ok; tile += gridDim.x) {
+        if (SYM) {
+          int m_blk, n_blk;
+          tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+          if (!sym_needed(m_blk, n_blk, p.r_rows, p.patches, p.n_images)) continue;
+        }
         if (!wait_bounded(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err)) {
           ok = false;
           break;
@@ -324,11 +369,13 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
     // ---------------------------------------------------------- epilogue
     const int et = threadIdx.x - 64;         // 0..127
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int P = p.patches;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end; tile += gridDim.x) {
       int m_blk, n_blk;
       tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+      if (SYM && !sym_needed(m_blk, n_blk, p.r_rows, P, p.n_images)) continue;
       const long long n0 = (long long)n_blk * BN;
       named_sync_epi();  // previous tile's readers are done with col_norm / col_w
       for (int j = et; j < BN; j += EPI_WARPS * 32) {
@@ -341,52 +388,86 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       if (named_sync_epi_any(*abort_flag)) break;  // uniform decision across the epilogue warps
       tc::fence_after_sync();
 
-      const long long row = (long long)m_blk * BM + quarter * 32 + lane;
+      const long long warp_row0 = (long long)m_blk * BM + quarter * 32;
+      const long long row = warp_row0 + lane;
       const bool row_ok = row < p.q_rows;
       const float qn = row_ok ? __ldg(p.q_norm + row) : 0.f;
       const float qi = row_ok ? __ldg(p.q_inv + row) : 0.f;
-      const int q_img = (int)((p.q_first_row + row) / p.patches);
-      int seg_img = (int)(n0 / p.patches);
-      long long seg_end = (long long)(seg_img + 1) * p.patches;
-      float m = FLT_MAX;
-      bool has = false;
+      const int q_img = (int)((p.q_first_row + row) / P);
+      // Symmetric mode keeps only columns of a later image than the row's.
+      const long long col_from = SYM ? (long long)(q_img + 1) * P : 0;
+      long long tile_last_row = (long long)m_blk * BM + BM - 1;
+      if (tile_last_row > p.q_rows - 1) tile_last_row = p.q_rows - 1;
+      const bool rows_full = (long long)m_blk * BM + BM <= p.q_rows;
+      const bool clean = !SYM || (rows_full && (tile_last_row / P) < (n0 / P));
+      // row images covered by this warp (symmetric column minima)
+      const bool warp_any = warp_row0 < p.q_rows;
+      long long warp_last = warp_row0 + 31;
+      if (warp_last > p.q_rows - 1) warp_last = p.q_rows - 1;
+      const int w_img0 = (int)(warp_row0 / P), w_img1 = warp_any ? (int)(warp_last / P) : w_img0 - 1;
+
+      int seg_img = (int)(n0 / P);
+      long long seg_end = (long long)(seg_img + 1) * P;
+      float m = INF;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         const long long c0 = n0 + chunk * 32;
         if (c0 >= p.r_rows) break;
-        uint32_t v[32];
-        tc::tmem_ld_32x32b_x32(tbase + (uint32_t)(chunk * 32), v);
+        uint32_t raw[32];
+        tc::tmem_ld_32x32b_x32(tbase + (uint32_t)(chunk * 32), raw);
         tc::tmem_wait_ld();
-        if (c0 + 32 <= seg_end && c0 + 32 <= p.r_rows) {
+        float v[32];
+        const bool full_chunk = c0 + 32 <= p.r_rows;
+        if (clean && full_chunk) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int jj = chunk * 32 + j;
-            const float d2 = fmaf(-__uint_as_float(v[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
-            m = fminf(m, d2);
+            v[j] = fmaf(-__uint_as_float(raw[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
           }
-          has = true;
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            const int jj = chunk * 32 + j;
             const long long col = c0 + j;
-            if (col < p.r_rows) {
-              if (col >= seg_end) {
-                if (has) flush_min(p, row_ok, row, q_img, seg_img, m);
-                ++seg_img;
-                seg_end += p.patches;
-                m = FLT_MAX;
-                has = false;
-              }
-              const int jj = chunk * 32 + j;
-              const float d2 = fmaf(-__uint_as_float(v[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
-              m = fminf(m, d2);
-              has = true;
+            const bool ok = row_ok && col < p.r_rows && col >= col_from;
+            v[j] = ok ? fmaf(-__uint_as_float(raw[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]) : INF;
+          }
+        }
+        // Row minima per reference-image segment.
+        if (c0 + 32 <= seg_end) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) m = fminf(m, v[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (c0 + j >= seg_end) {
+              if (row_ok && seg_img != q_img) flush_min(p, row, seg_img, m);
+              ++seg_img;
+              seg_end += P;
+              m = INF;
+            }
+            m = fminf(m, v[j]);
+          }
+        }
+        if (SYM) {
+          // Column minima over this warp's rows, one per row image.
+          const long long col = c0 + lane;
+          if (w_img0 == w_img1) {
+            const float cm = warp_column_min(v, lane);
+            if (col < p.r_rows) flush_min(p, col, w_img0, cm);
+          } else {
+            for (int ri = w_img0; ri <= w_img1; ++ri) {
+              float u[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) u[j] = (q_img == ri) ? v[j] : INF;
+              const float cm = warp_column_min(u, lane);
+              if (col < p.r_rows) flush_min(p, col, ri, cm);
             }
           }
         }
       }
-      if (has) flush_min(p, row_ok, row, q_img, seg_img, m);
+      if (row_ok && seg_img != q_img) flush_min(p, row, seg_img, m);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.acc_empty[acc]));
@@ -530,6 +611,71 @@ int trimmed_rows_per_block(int n) {
 
 }  // namespace
 
+// Balanced split of the symmetric tile list.  Tiles are visited in the
+// kernel's linear order (groups of GROUP_M m-tiles, n outer, m inner); the
+// needed tiles of one (group, n) column are counted in closed form from
+// n_start(m), the first n-tile holding a column of a later image than the
+// m-tile's first row.  Part k starts at the first column whose preceding
+// count reaches total * k / parts.
+static void sym_part_range(long long rows, int patches, int n_images, int num_m, int num_n, int part,
+                           int parts, long long* tile_begin, long long* tile_end) {
+  using namespace nearest;
+  std::vector<int> n_start(num_m);
+  for (int m = 0; m < num_m; ++m) {
+    const long long img = (long long)m * BM / patches;
+    if (img >= n_images - 1) {
+      n_start[m] = num_n;
+    } else {
+      const long long need = (img + 1) * patches - BN + 1;  // n*BN + BN - 1 >= (img+1)*P
+      n_start[m] = need <= 0 ? 0 : (int)((need + BN - 1) / BN);
+    }
+  }
+  const int groups = (num_m + GROUP_M - 1) / GROUP_M;
+  long long total = 0;
+  for (int m = 0; m < num_m; ++m) total += num_n - n_start[m];
+  const long long lin_total = (long long)num_m * num_n;
+  auto start_of = [&](int k) -> long long {
+    if (k <= 0) return 0;
+    if (k >= parts) return lin_total;
+    const long long target = total * k / parts;
+    long long acc = 0;
+    for (int g = 0; g < groups; ++g) {
+      const int first_m = g * GROUP_M;
+      const int gm = std::min(GROUP_M, num_m - first_m);
+      int ptr = first_m;  // m in [first_m, ptr) have n_start <= n
+      for (int n = 0; n < num_n; ++n) {
+        while (ptr < first_m + gm && n_start[ptr] <= n) ++ptr;
+        if (acc >= target) return (long long)g * GROUP_M * num_n + (long long)n * gm;
+        acc += ptr - first_m;
+      }
+    }
+    return lin_total;
+  };
+  *tile_begin = start_of(part);
+  *tile_end = start_of(part + 1);
+}
+
+static int set_smem_attr() {
+  static std::mutex m;
+  static bool done[64] = {false};
+  int dev = 0;
+  MUSC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(m);
+  if (dev >= 64 || !done[dev]) {
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)nearest::SMEM_BYTES));
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)nearest::SMEM_BYTES));
+    if (dev < 64) done[dev] = true;
+  }
+  return MUSC_B200_OK;
+}
+
+static int fill_table(float* table, long long count, cudaStream_t s) {
+  fill_u32_kernel<<<1184, 256, 0, s>>>(reinterpret_cast<unsigned int*>(table), count, 0x7F7FFFFFu);
+  return check_launch("fill_u32_kernel");
+}
+
 int nearest_launch(const void* query_bank, long long query_rows, long long query_first_row,
                    const void* ref_bank, long long ref_rows, int channels, int patches,
                    float* nearest_sq, cudaStream_t s) {
@@ -543,9 +689,7 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   MUSC_TRY(make_plane_map(&mrh, rb + rl.hi, ref_rows, channels, nearest::BN));
   MUSC_TRY(make_plane_map(&mrl, rb + rl.lo, ref_rows, channels, nearest::BN));
   const int n_images = (int)(ref_rows / patches);
-  const long long table = (long long)n_images * query_rows;
-  fill_u32_kernel<<<1184, 256, 0, s>>>(reinterpret_cast<unsigned int*>(nearest_sq), table, 0x7F7FFFFFu);
-  MUSC_TRY(check_launch("fill_u32_kernel"));
+  MUSC_TRY(fill_table(nearest_sq, (long long)n_images * query_rows, s));
   nearest::Params p;
   p.q_norm = reinterpret_cast<const float*>(qb + ql.norm);
   p.q_inv = reinterpret_cast<const float*>(qb + ql.inv);
@@ -557,23 +701,54 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   p.q_rows = query_rows;
   p.r_rows = ref_rows;
   p.q_first_row = query_first_row;
+  p.rows_per_block = query_rows;
+  p.blocked = 0;
   p.patches = patches;
+  p.n_images = n_images;
   p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
   p.num_m = (int)((query_rows + nearest::BM - 1) / nearest::BM);
   p.num_n = (int)((ref_rows + nearest::BN - 1) / nearest::BN);
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  MUSC_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !attr_set[dev]) {
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)nearest::SMEM_BYTES));
-    attr_set[dev] = true;
-  }
-  const long long tiles = (long long)p.num_m * p.num_n;
-  if (tiles > 0x7FFFFFFFLL) return fail(MUSC_B200_ERR_INVALID, "nearest: too many tiles");
-  const int grid = (int)std::min<long long>(tiles, sm_count());
-  nearest::nearest_kernel<<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mqh, mql, mrh, mrl, p);
-  return check_launch("nearest_kernel");
+  p.tile_begin = 0;
+  p.tile_end = (long long)p.num_m * p.num_n;
+  MUSC_TRY(set_smem_attr());
+  const int grid = (int)std::min<long long>(p.tile_end, sm_count());
+  nearest::nearest_kernel<false><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mqh, mql, mrh, mrl, p);
+  return check_launch("nearest_kernel<directed>");
+}
+
+int nearest_pool_launch(const void* bank, long long rows, int channels, int patches, int part, int parts,
+                        long long rows_per_block, float* nearest_sq, cudaStream_t s) {
+  const BankLayout l = bank_layout(rows, channels);
+  const uint8_t* b = static_cast<const uint8_t*>(bank);
+  CUtensorMap mah, mal, mbh, mbl;
+  MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, nearest::BM));
+  MUSC_TRY(make_plane_map(&mal, b + l.lo, rows, channels, nearest::BM));
+  MUSC_TRY(make_plane_map(&mbh, b + l.hi, rows, channels, nearest::BN));
+  MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, nearest::BN));
+  const int n_images = (int)(rows / patches);
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  MUSC_TRY(fill_table(nearest_sq, blocks * n_images * rows_per_block, s));
+  nearest::Params p;
+  p.q_norm = p.r_norm = reinterpret_cast<const float*>(b + l.norm);
+  p.q_inv = p.r_inv = reinterpret_cast<const float*>(b + l.inv);
+  p.nearest = reinterpret_cast<unsigned int*>(nearest_sq);
+  p.err = device_error_ptr();
+  if (!p.err) return fail(MUSC_B200_ERR_CUDA, "nearest_pool: device error word unavailable");
+  p.q_rows = p.r_rows = rows;
+  p.q_first_row = 0;
+  p.rows_per_block = rows_per_block;
+  p.blocked = blocks > 1 ? 1 : 0;
+  p.patches = patches;
+  p.n_images = n_images;
+  p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
+  p.num_m = (int)((rows + nearest::BM - 1) / nearest::BM);
+  p.num_n = (int)((rows + nearest::BN - 1) / nearest::BN);
+  sym_part_range(rows, patches, n_images, p.num_m, p.num_n, part, parts, &p.tile_begin, &p.tile_end);
+  if (p.tile_end <= p.tile_begin) return MUSC_B200_OK;  // nothing to do for this part
+  MUSC_TRY(set_smem_attr());
+  const int grid = (int)std::min<long long>(p.tile_end - p.tile_begin, sm_count());
+  nearest::nearest_kernel<true><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mah, mal, mbh, mbl, p);
+  return check_launch("nearest_kernel<symmetric>");
 }
 
 int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, int rank_lo, int rank_hi,
@@ -634,6 +809,33 @@ extern "C" int musc_b200_nearest(const void* query_bank, long long query_rows, l
                         patches_per_image, nearest_sq, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" size_t musc_b200_nearest_pool_bytes(long long rows, int patches_per_image,
+                                               long long rows_per_block) {
+  if (rows <= 0 || patches_per_image <= 0 || rows_per_block <= 0) return 0;
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  return (size_t)blocks * (size_t)(rows / patches_per_image) * (size_t)rows_per_block * sizeof(float);
+}
+
+extern "C" int musc_b200_nearest_pool(const void* bank, long long rows, int channels, int patches_per_image,
+                                      int part, int n_parts, long long rows_per_block, float* nearest_sq,
+                                      musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(rows, channels));
+  if (!bank || !nearest_sq) return fail(MUSC_B200_ERR_INVALID, "nearest_pool: null pointer");
+  if (reinterpret_cast<uintptr_t>(bank) % 1024 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest_pool: bank must be 1024-byte aligned");
+  if (patches_per_image <= 0 || rows % patches_per_image != 0 || rows / patches_per_image < 2)
+    return fail(MUSC_B200_ERR_INVALID, "nearest_pool: rows must hold N >= 2 whole images");
+  if (n_parts <= 0 || part < 0 || part >= n_parts)
+    return fail(MUSC_B200_ERR_INVALID, "nearest_pool: requires 0 <= part < n_parts");
+  if (rows_per_block <= 0 || rows_per_block % patches_per_image != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest_pool: rows_per_block must be a positive multiple of P");
+  if (reinterpret_cast<uintptr_t>(nearest_sq) % 4 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "nearest_pool: output must be 4-byte aligned");
+  MUSC_TRY(require_sm100());
+  return nearest_pool_launch(bank, rows, channels, patches_per_image, part, n_parts, rows_per_block,
+                             nearest_sq, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
                                       int rank_lo, int rank_hi, double* scores, musc_b200_stream stream) {
   if (!nearest_sq || !scores) return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: null pointer");
@@ -669,6 +871,6 @@ extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, i
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* table = reinterpret_cast<float*>(ws + bank_size);
   MUSC_TRY(musc_b200_prep_bank(z, rows, c, ws, bank_size, stream));
-  MUSC_TRY(musc_b200_nearest(ws, rows, 0, ws, rows, c, p, table, stream));
+  MUSC_TRY(musc_b200_nearest_pool(ws, rows, c, p, 0, 1, rows, table, stream));
   return musc_b200_trimmed_mean(table, rows, n, rank_lo, rank_hi, scores, stream);
 }

@@ -169,6 +169,27 @@ def nearest(query_bank: torch.Tensor, query_rows: int, query_first_row: int, ref
     return out
 
 
+def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part: int = 0,
+                 parts: int = 1, rows_per_block: int | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Symmetric pool minima: ``(blocks, n_images, rows_per_block)`` squared, FLT_MAX where unset.
+
+    Evaluates part ``part`` of ``parts`` of the pool's symmetric tile list;
+    with one part the single block is the full ``(n_images, rows)`` table.
+    """
+    dev = bank.device
+    rpb = rows if rows_per_block is None else rows_per_block
+    n_images = rows // patches
+    blocks = -(-rows // rpb)
+    if out is None:
+        out = torch.empty(blocks, n_images, rpb, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_nearest_pool(_ptr(bank), rows, channels, patches, part, parts, rpb,
+                                               _ptr(out), _stream(dev))
+        _lib.check(st, 'musc_b200_nearest_pool')
+    return out
+
+
 def trimmed_mean(nearest_sq: torch.Tensor, rank_lo: int, rank_hi: int,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     """Interval average of ``sqrt(nearest_sq)`` over images -> ``(query_rows,)`` float64."""

@@ -11,10 +11,12 @@ This is the scoring half of ``MuSc.make_category_data``
 * layer and radius means, up-sampling and image maxima (``:259-288``).
 
 Multi-GPU (one process per GPU): rank r owns the query images
-``[r*ceil(N/G), ...)``, aggregates only those, all-gathers each bank over NCCL
-(overlapped with the previous bank's GEMM) and scores its query rows against
-the whole pool; self exclusion uses global image indices.  The reference is
-single-device; the sharding is this library's addition.
+``[r*ceil(N/G), ...)`` and aggregates only those; each bank is all-gathered
+over NCCL (overlapped with the previous bank's work), every rank evaluates a
+balanced share of the pool's symmetric distance tiles, and a MIN
+reduce-scatter of the nearest table gives each rank the minima of its own
+query rows.  The reference is single-device; the sharding is this library's
+addition.
 """
 from __future__ import annotations
 
@@ -97,12 +99,18 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         else:
             kernels.lnamd(t, radii, True, out=[local[li, ri, :n_local] for ri in range(n_r)])
 
-    # 2. Per bank: (gather), prep, nearest, interval average.
+    # 2. Per bank: (gather), prep, symmetric nearest minima, interval average.
+    #    Rank r evaluates part r of the pool's symmetric tile list into a table
+    #    whose blocks are the ranks' query rows; a MIN reduce-scatter hands each
+    #    rank the minima of its own rows.
     banks = [(li, ri) for ri in range(n_r) for li in range(n_l)]
     scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
     rows = n_images * p
     q_rows = n_local * p
-    nearest_buf = torch.empty(n_images, max(q_rows, 1), dtype=torch.float32, device=dev)
+    rpb = per * p if world > 1 else rows
+    table = torch.empty(world if world > 1 else 1, n_images, rpb, dtype=torch.float32, device=dev)
+    mine = torch.empty(n_images, rpb, dtype=torch.float32, device=dev) if world > 1 else table[0]
+    block_scores = torch.empty(rpb, dtype=torch.float64, device=dev)
     if world > 1:
         full = [torch.empty(world * per, p, c, dtype=torch.float32, device=dev) for _ in range(2)]
         works = [None] * len(banks)
@@ -118,14 +126,16 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         else:
             z_full = local[li, ri, :n_images]
         bank = kernels.prep_bank(z_full.reshape(rows, c))
+        kernels.nearest_pool(bank, rows, c, p, rank, world, rpb, out=table)
+        if world > 1:
+            _min_reduce_scatter(table, mine, rank, group)
         if q_rows == 0:
             continue
-        if world > 1:
-            qbank = kernels.prep_bank(local[li, ri, :n_local].reshape(q_rows, c))
+        if q_rows == rpb:
+            kernels.trimmed_mean(mine, a, b, out=scores[ri, li].view(-1))
         else:
-            qbank = bank
-        near = kernels.nearest(qbank, q_rows, first * p, bank, rows, c, p, out=nearest_buf)
-        kernels.trimmed_mean(near, a, b, out=scores[ri, li].view(-1))
+            kernels.trimmed_mean(mine, a, b, out=block_scores)
+            scores[ri, li].view(-1).copy_(block_scores[:q_rows])
 
     # 3. Layer/radius means, up-sampling, image maxima for the local images.
     if n_local:
@@ -134,6 +144,16 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         maps = torch.empty(0, side, side, dtype=torch.float64, device=dev)
         image_max = torch.empty(0, dtype=torch.float64, device=dev)
     return PoolScores(scores, maps, image_max, first, n_images)
+
+
+def _min_reduce_scatter(table: torch.Tensor, out: torch.Tensor, rank: int, group) -> None:
+    """Element-wise MIN over ranks of ``table`` (G, N, rpb); rank r keeps block r."""
+    import torch.distributed as dist
+    if dist.get_backend(group) == 'nccl':
+        dist.reduce_scatter_tensor(out, table, op=dist.ReduceOp.MIN, group=group)
+    else:  # gloo (CPU tests of the sharding logic) has no reduce-scatter
+        dist.all_reduce(table, op=dist.ReduceOp.MIN, group=group)
+        out.copy_(table[rank])
 
 
 def gather_pool(result: PoolScores, group=None) -> tuple[torch.Tensor, torch.Tensor]:

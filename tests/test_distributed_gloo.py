@@ -1,0 +1,120 @@
+"""Multi-rank sharding logic on CPU: world_size 2 (and 3) gloo ranks.
+
+``musc_b200.pipeline.score_pool`` is run with the numpy oracle substituted for
+the CUDA operator set, so the test exercises exactly the host logic of the
+multi-GPU path -- the query-image partition, the per-rank LNAMD, the bank
+all-gather, the split of the symmetric distance work into per-rank parts, the
+MIN reduction of the nearest tables and the score assembly -- and checks the
+gathered maps and image maxima against the single-process result bit for bit.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from musc_b200 import ops
+from musc_b200.pipeline import gather_pool, score_pool, shard_range
+from oracle import lnamd as olnamd
+from oracle import reduce as oreduce
+
+N_IMAGES, SIDE, C, LAYERS, RADII = 5, 7, 32, 2, (1, 3)
+
+
+class OracleKernels:
+    """The pipeline's operator set, evaluated by the numpy oracle on CPU tensors."""
+
+    trimmed_ranks = staticmethod(ops.trimmed_ranks)
+
+    @staticmethod
+    def lnamd(tokens, radii, l2_normalize, out):
+        for r, o in zip(radii, out):
+            z = olnamd.bank(tokens.numpy(), r) if l2_normalize else olnamd.lnamd(tokens.numpy(), r)
+            o.copy_(torch.from_numpy(z))
+
+    @staticmethod
+    def lnamd_super_fast(tokens, side, l2_normalize, out, image_stride, patch_stride):
+        z = olnamd.lnamd_super_fast(tokens.numpy(), side)
+        out.copy_(torch.from_numpy(olnamd.l2_normalize(z) if l2_normalize else z))
+
+    @staticmethod
+    def prep_bank(z):
+        return z.clone()
+
+    @staticmethod
+    def nearest_pool(bank, rows, c, p, part, parts, rpb, out):
+        """Squared minima for the image pairs {i, j} with min(i, j) % parts == part."""
+        n = rows // p
+        z = bank.numpy().reshape(n, p, c).astype(np.float64)
+        out.fill_(float(np.finfo(np.float32).max))
+        for i in range(n):
+            for j in range(n):
+                if i == j or min(i, j) % parts != part:
+                    continue
+                d2 = ((z[i][:, None, :] - z[j][None, :, :]) ** 2).sum(-1).min(1)  # rows of i vs image j
+                for q in range(p):
+                    row = i * p + q
+                    out[row // rpb, j, row % rpb] = float(np.float32(d2[q]))
+        return out
+
+    @staticmethod
+    def trimmed_mean(near, a, b, out):
+        d = np.sort(np.sqrt(near.numpy().astype(np.float64)), axis=0)[a:b]
+        out.copy_(torch.from_numpy(d.mean(axis=0).astype(np.float32).astype(np.float64)))
+        return out
+
+    @staticmethod
+    def score_maps(scores, image_size):
+        maps, mx = oreduce.image_scores(scores.numpy(), image_size)
+        return torch.from_numpy(maps), torch.from_numpy(mx), None
+
+
+def _tokens():
+    g = torch.Generator().manual_seed(21)
+    return [torch.randn(N_IMAGES, 1 + SIDE * SIDE, C, generator=g) for _ in range(LAYERS)]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, queue):
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        first, end, _ = shard_range(N_IMAGES, world, rank)
+        local = [t[first:end].contiguous() for t in _tokens()]
+        res = score_pool(local, n_images=N_IMAGES, radii=RADII, image_size=40, group=dist.group.WORLD,
+                         kernels=OracleKernels())
+        maps, mx = gather_pool(res, dist.group.WORLD)
+        if rank == 0:
+            queue.put((maps.numpy(), mx.numpy(), res.scores.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize('world', [2, 3])
+def test_sharded_pool_equals_single_process(world):
+    single = score_pool(_tokens(), radii=RADII, image_size=40, kernels=OracleKernels())
+    ctx = mp.get_context('spawn')
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    maps, mx, scores0 = queue.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    np.testing.assert_array_equal(maps, single.maps.numpy())
+    np.testing.assert_array_equal(mx, single.image_max.numpy())
+    first, end, _ = shard_range(N_IMAGES, world, 0)
+    np.testing.assert_array_equal(scores0, single.scores.numpy()[:, :, first:end])

@@ -113,12 +113,46 @@ def test_nearest_query_slices_are_bit_identical(cuda_device):
         assert torch.equal(part, full[:, first_img * p:(first_img + count) * p])
 
 
+@pytest.mark.parametrize('n,p,c', [(6, 49, 64), (11, 1369, 64), (4, 300, 1024)])
+def test_symmetric_pool_table_matches_directed(cuda_device, n, p, c):
+    """Each unordered pair evaluated once gives the same minima as the directed kernel."""
+    from musc_b200 import ops
+    z = torch.randn(n * p, c, generator=torch.Generator().manual_seed(n + p)).to(cuda_device)
+    bank = ops.prep_bank(z)
+    directed = ops.nearest(bank, n * p, 0, bank, n * p, c, p)
+    sym = ops.nearest_pool(bank, n * p, c, p)[0]
+    assert torch.equal(sym == torch.finfo(torch.float32).max, directed == torch.finfo(torch.float32).max)
+    torch.testing.assert_close(sym, directed, rtol=2e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize('parts', [2, 3, 8])
+def test_symmetric_parts_combine_exactly(cuda_device, parts):
+    """Per-rank parts of the tile list, MIN-combined, equal the one-part table bit for bit,
+    including the rank-blocked layout used by the reduce-scatter."""
+    from musc_b200 import ops
+    from musc_b200.pipeline import shard_range
+    n, p, c = 13, 1369, 64
+    z = torch.randn(n * p, c, generator=torch.Generator().manual_seed(parts)).to(cuda_device)
+    bank = ops.prep_bank(z)
+    whole = ops.nearest_pool(bank, n * p, c, p)[0]
+    _, _, per = shard_range(n, parts, 0)
+    rpb = per * p
+    combined = None
+    for k in range(parts):
+        t = ops.nearest_pool(bank, n * p, c, p, k, parts, rpb)          # (parts, n, rpb)
+        combined = t if combined is None else torch.minimum(combined, t)
+    # un-block: row = blk * rpb + r
+    blocks = combined.shape[0]                                          # ceil(rows / rpb)
+    flat = combined.permute(1, 0, 2).reshape(n, blocks * rpb)[:, :n * p]
+    assert torch.equal(flat, whole)
+
+
 def test_trimmed_mean_ties_and_offsets(cuda_device):
     from musc_b200 import ops
     gen = torch.Generator().manual_seed(5)
     n, rows = 37, 5000
     vals = (torch.randint(0, 6, (n, rows), generator=gen).float() * 0.25 + 1.0) ** 2  # many exact ties
-    vals[torch.randint(0, n, (rows,), generator=gen), torch.arange(rows)] = np.finfo(np.float32).max
+    vals[torch.randint(0, n, (rows,), generator=gen), torch.arange(rows)] = float(np.finfo(np.float32).max)
     for lo, hi in [(0, 10), (3, 11), (0, 36), (35, 36)]:
         got = ops.trimmed_mean(vals.to(cuda_device), lo, hi).cpu().numpy()
         d = np.sort(np.sqrt(vals.numpy().astype(np.float64)), axis=0)[lo:hi]
