@@ -82,6 +82,29 @@ int musc_b200_lnamd(const void* tokens, int dtype, int n_images, int tokens_per_
                     long long out_image_stride, long long out_patch_stride, int l2_normalize,
                     void* workspace, size_t workspace_bytes, musc_b200_stream stream);
 
+/* musc_b200_lnamd without a workspace argument, for callers that cannot
+ * allocate device memory: hosts that hand the library only the tensors they
+ * already own -- a plug-in inside another runtime's memory arena, a service
+ * that forbids device allocation after start-up, or a foreign-language caller
+ * with no CUDA allocator of its own.  This entry point has no counterpart in
+ * the reference.  Its scratch (the per-image LayerNorm sums) is a 256 KB
+ * array in the library's static device memory, so:
+ *   - at most 2048 images per call; larger n_images returns
+ *     MUSC_B200_ERR_INVALID before any work is enqueued;
+ *   - the first call on a device looks the array's address up for that
+ *     device (cudaGetSymbolAddress) -- make that first call before any stream
+ *     capture on the device;
+ *   - every call shares the one array: nothing in it needs to start at zero
+ *     (each call overwrites the slots it reads before reading them), but calls
+ *     that overlap on the GPU -- concurrent streams, or other host threads --
+ *     race on it; serialise them.
+ * Inputs, outputs and results are exactly those of musc_b200_lnamd.  No
+ * cudaMalloc, cudaFree or allocating library routine is called. */
+int musc_b200_lnamd_noalloc(const void* tokens, int dtype, int n_images, int tokens_per_image,
+                            int channels, int n_radii, const int* radii, float* const* out,
+                            long long out_image_stride, long long out_patch_stride, int l2_normalize,
+                            musc_b200_stream stream);
+
 /* Super-fast profile: r = 3 LNAMD on the side x side grid, then
  * adaptive_avg_pool2d to out_side x out_side (fp32), then optional L2
  * normalisation.  Replaces SuperFastAggregation.__call__

@@ -23,6 +23,9 @@
 // written.
 #include "common.cuh"
 
+#include <mutex>
+#include <vector>
+
 namespace musc {
 
 constexpr int kStatSplit = 8;
@@ -411,4 +414,54 @@ extern "C" int musc_b200_lnamd_super_fast(const void* tokens, int dtype, int n_i
       break;
   }
   return check_launch("lnamd_super_fast_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// musc_b200_lnamd_noalloc: the same LNAMD call for callers that cannot
+// allocate device memory.  Its only scratch -- the per-image LayerNorm
+// partial sums, 16 doubles per image -- lives in this file-scope device array,
+// so the call allocates nothing.  Every GPU that loads the library holds the
+// array (256 KB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxImages = 2048;
+__device__ __align__(256) double g_lnamd_noalloc_scratch[kNoAllocMaxImages * kStatSplit * 2];
+
+// Device address of the scratch array on the current device.  Host code may
+// not pass the array's name to a kernel (on the host it is only a stand-in
+// symbol), so the address is looked up once per device with that device
+// current and cached.
+int noalloc_scratch(double** out) {
+  static std::mutex m;
+  static std::vector<double*> ptrs;
+  int dev = 0;
+  MUSC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(m);
+  if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&p, g_lnamd_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(g_lnamd_noalloc_scratch)");
+    ptrs[dev] = static_cast<double*>(p);
+  }
+  *out = ptrs[dev];
+  return MUSC_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int musc_b200_lnamd_noalloc(const void* tokens, int dtype, int n_images, int tokens_per_image,
+                                       int channels, int n_radii, const int* radii, float* const* out,
+                                       long long out_image_stride, long long out_patch_stride,
+                                       int l2_normalize, musc_b200_stream stream) {
+  if (n_images > kNoAllocMaxImages)
+    return fail(MUSC_B200_ERR_INVALID,
+                "lnamd_noalloc: n_images exceeds the static scratch limit of 2048 images per call "
+                "(split the batch, or use musc_b200_lnamd with a workspace)");
+  double* scratch = nullptr;
+  MUSC_TRY(noalloc_scratch(&scratch));
+  return musc_b200_lnamd(tokens, dtype, n_images, tokens_per_image, channels, n_radii, radii, out,
+                         out_image_stride, out_patch_stride, l2_normalize, scratch,
+                         sizeof(g_lnamd_noalloc_scratch), stream);
 }

@@ -28,6 +28,8 @@ SIGNATURES = {
     'musc_b200_lnamd_workspace_bytes': (_sz, [_int]),
     'musc_b200_lnamd': (_int, [_vp, _int, _int, _int, _int, _int, ctypes.POINTER(_int),
                                ctypes.POINTER(_vp), _ll, _ll, _int, _vp, _sz, _vp]),
+    'musc_b200_lnamd_noalloc': (_int, [_vp, _int, _int, _int, _int, _int, ctypes.POINTER(_int),
+                                       ctypes.POINTER(_vp), _ll, _ll, _int, _vp]),
     'musc_b200_lnamd_super_fast': (_int, [_vp, _int, _int, _int, _int, _int, _vp, _ll, _ll, _int,
                                           _vp, _sz, _vp]),
     'musc_b200_bank_bytes': (_sz, [_ll, _int]),
