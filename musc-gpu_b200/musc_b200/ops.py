@@ -248,3 +248,35 @@ def score_maps(scores: torch.Tensor, image_size: int = 518, upsampled: bool = Fa
                                              _ptr(image_max), _ptr(up), _stream(dev))
         _lib.check(st, 'musc_b200_score_maps')
     return maps, image_max, up
+
+
+# --------------------------------------------------------------------------- attention
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``softmax(q k^T * scale) v`` per head for token-major bf16 ``(B, L, heads*64)`` views.
+
+    ``q``, ``k``, ``v`` may be column slices of one packed QKV projection (same row
+    stride); the result is ``(B, L, heads*64)`` bf16.
+    """
+    _require_cuda(q, 'attention')
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError('attention: q, k, v must be bfloat16')
+    if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError('attention: q, k, v must share shape (B, L, heads*head_dim)')
+    b, length, width = q.shape
+    head_dim = width // heads
+    if head_dim * heads != width:
+        raise ValueError('attention: width must be heads * head_dim')
+    for t in (q, k, v):
+        if t.stride(2) != 1 or t.stride(0) != length * t.stride(1) or t.stride(1) != q.stride(1):
+            raise ValueError('attention: q, k, v must be token-major with one common row stride')
+    if out is None:
+        out = torch.empty(b, length, width, dtype=torch.bfloat16, device=q.device)
+    scale = head_dim ** -0.5 if scale is None else scale
+    dev = q.device
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_attention_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, length, heads,
+                                                head_dim, q.stride(1), out.stride(1), float(scale),
+                                                _stream(dev))
+        _lib.check(st, 'musc_b200_attention_fwd')
+    return out
