@@ -194,14 +194,16 @@ int musc_b200_score_maps(const double* scores, int n_radii, int n_layers, int n,
  * blocks call it (models/backbone/open_clip/transformer.py:221-234), with the
  * reference's row-softmax kernel (models/modules/_attention_gpu.py:41-81)
  * fused in: the tokens x tokens logits never reach memory.
- * q, k, v: bf16, element (b, t, h, d) at base[(b * tokens + t) * qkv_row_stride
+ * q, k, v: fp16 or bf16 (dtype MUSC_B200_F16 / MUSC_B200_BF16), element
+ * (b, t, h, d) at base[(b * tokens + t) * qkv_row_stride
  * + h * head_dim + d] (so the three slices of one packed QKV projection are
  * addressed by base, base + heads*head_dim, base + 2*heads*head_dim);
- * out: bf16, same addressing with out_row_stride.  head_dim == 64; strides
+ * out: same type, same addressing with out_row_stride.  Softmax and
+ * accumulation in fp32; P is rounded to the input type for the second MMA.  head_dim == 64; strides
  * multiples of 8 elements; pointers 16-byte aligned.
  * ---------------------------------------------------------------------- */
-int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* out, int batch,
-                            int tokens, int heads, int head_dim, long long qkv_row_stride,
+int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* out, int dtype,
+                            int batch, int tokens, int heads, int head_dim, long long qkv_row_stride,
                             long long out_row_stride, float scale, musc_b200_stream stream);
 
 #ifdef __cplusplus

@@ -5,18 +5,18 @@
 // (models/modules/_attention_gpu.py:41-81) fused in, so the (L x L) logits and
 // probabilities never reach memory.
 //
-// One CTA per (batch, head, 128-query tile); head_dim 64, bf16 in/out, fp32
-// accumulation.  Warp roles:
+// One CTA per (batch, head, 128-query tile); head_dim 64, fp16 or bf16 in/out
+// (both operands of every MMA share the type), fp32 softmax and accumulation.  Warp roles:
 //   warp 0     TMA: Q once, then K_j / V_j tiles of 128 keys into 2-deep rings;
 //   warp 1     one thread issues tcgen05.mma: S_j = Q K_j^T (128x128x64) into a
 //              double-buffered TMEM S, and PV_j = P_j V_j (128x64x128) into a
 //              double-buffered TMEM PV (V is the MN-major B operand);
 //   warps 2-5  softmax, one thread per query row: tcgen05.ld of S_j, online
-//              max / exp2 / row sum in fp32, P_j written to shared memory as
-//              bf16 in the K-major 128-byte swizzle layout the MMA reads; one
+//              max / exp2 / row sum in fp32, P_j written to shared memory in
+//              the input type, K-major 128-byte swizzle layout the MMA reads; one
 //              tile later the same thread reads PV_j and accumulates
 //              O = O * alpha_j + PV_j in registers (so the tensor core never
-//              waits for a rescale); finally O / l goes out as bf16.
+//              waits for a rescale); finally O / l goes out in the input type.
 // QK_{j+1} overlaps softmax_j; PV_j overlaps softmax_{j+1}.
 // Algorithmic work: 4 * L^2 * d flop per (batch, head); L^2 exponentials.
 #include "common.cuh"
@@ -41,8 +41,11 @@ constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0;      // S buffers at columns 0 and 128
 constexpr int PV_COL = 256;   // PV buffers at columns 256 and 320
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
-constexpr uint32_t IDESC_QK = tc::idesc_f16(BQ, BKV, /*bf16*/ 1);
-constexpr uint32_t IDESC_PV = tc::idesc_f16(BQ, D, /*bf16*/ 1) | (1u << 16);  // B (V) MN-major
+// kind::f16 operand format: 0 = fp16, 1 = bf16 (A and B always share it).
+template <bool FP16> constexpr uint32_t idesc_qk() { return tc::idesc_f16(BQ, BKV, FP16 ? 0 : 1); }
+template <bool FP16> constexpr uint32_t idesc_pv() {
+  return tc::idesc_f16(BQ, D, FP16 ? 0 : 1) | (1u << 16);  // B (V) MN-major
+}
 
 struct Smem {
   uint8_t q[TILE_BYTES];
@@ -62,7 +65,7 @@ struct Smem {
 constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
 
 struct Params {
-  __nv_bfloat16* out;
+  void* out;
   long long out_row_stride;  // elements between consecutive tokens of out
   int* err;
   int tokens, heads, n_q_tiles, n_kv;
@@ -100,11 +103,18 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&t);
+template <bool FP16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if (FP16) {
+    __half2 t = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&t);
+  } else {
+    __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&t);
+  }
 }
 
+template <bool FP16>
 __global__ void __launch_bounds__(THREADS, 1)
 attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                  const __grid_constant__ CUtensorMap map_v, const Params p) {
@@ -211,7 +221,7 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
 #pragma unroll
           for (int k16 = 0; k16 < D / 16; ++k16)
             tc::mma_f16_ss(d_tmem, tc::desc_k_sw128(q_addr + k16 * 32), tc::desc_k_sw128(k_addr + k16 * 32),
-                           IDESC_QK, k16 ? 1u : 0u);
+                           idesc_qk<FP16>(), k16 ? 1u : 0u);
           tc::mma_commit(tc::smem_u32(&sm.k_empty[s]));
           tc::mma_commit(tc::smem_u32(&sm.s_full[sb]));
         }
@@ -234,7 +244,7 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
           for (int k16 = 0; k16 < BKV / 16; ++k16) {
             const uint32_t pa = p_addr + (uint32_t)((k16 >> 2) * (BQ * 128) + (k16 & 3) * 32);
             const uint32_t va = v_addr + (uint32_t)(k16 * 2048);  // 16 keys = two 8-key groups
-            tc::mma_f16_ss(d_tmem, tc::desc_k_sw128(pa), desc_mn_sw128(va), IDESC_PV, k16 ? 1u : 0u);
+            tc::mma_f16_ss(d_tmem, tc::desc_k_sw128(pa), desc_mn_sw128(va), idesc_pv<FP16>(), k16 ? 1u : 0u);
           }
           tc::mma_commit(tc::smem_u32(&sm.v_empty[s]));
           tc::mma_commit(tc::smem_u32(&sm.o_full[pb]));
@@ -297,8 +307,8 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
             e[t] = c < valid ? ex2(sv[c] - m_new) : 0.f;
             lsum += e[t];
           }
-          uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]),
-                                pack_bf16(e[6], e[7]));
+          uint4 pk = make_uint4(pack2<FP16>(e[0], e[1]), pack2<FP16>(e[2], e[3]), pack2<FP16>(e[4], e[5]),
+                                pack2<FP16>(e[6], e[7]));
           const int blk = ch >> 3, cc = ch & 7;  // 64-key column block, chunk within the 128-byte row
           *reinterpret_cast<uint4*>(prow_base + blk * (BQ * 128) + ((cc ^ (r & 7)) << 4)) = pk;
         }
@@ -347,13 +357,13 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
     const int token = q_tile * BQ + r;
     if (ok && token < p.tokens) {
       const float inv = 1.f / l_run;
-      __nv_bfloat16* dst = p.out + ((long long)b * p.tokens + token) * p.out_row_stride + h * D;
+      uint16_t* dst = static_cast<uint16_t*>(p.out) + ((long long)b * p.tokens + token) * p.out_row_stride + h * D;
 #pragma unroll
       for (int c8 = 0; c8 < D / 8; ++c8) {
-        uint4 pk = make_uint4(pack_bf16(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv),
-                              pack_bf16(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
-                              pack_bf16(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
-                              pack_bf16(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+        uint4 pk = make_uint4(pack2<FP16>(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv),
+                              pack2<FP16>(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
+                              pack2<FP16>(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
+                              pack2<FP16>(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
         *reinterpret_cast<uint4*>(dst + c8 * 8) = pk;
       }
     }
@@ -394,14 +404,16 @@ int encode_fn(EncodeTiledFn* fn) {
 
 // bf16 [rows][row_stride] with the head slices as the inner dimension; box = one head
 // (64 elements = 128 bytes) x 128 token rows, 128-byte swizzle.
-int make_token_map(CUtensorMap* map, const void* base, long long rows, int inner, long long row_stride) {
+int make_token_map(CUtensorMap* map, const void* base, long long rows, int inner, long long row_stride,
+                   bool fp16) {
   EncodeTiledFn encode;
   MUSC_TRY(encode_fn(&encode));
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
   cuuint32_t box[2] = {(cuuint32_t)attn::D, (cuuint32_t)attn::BKV};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  CUresult r = encode(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                      const_cast<void*>(base), dims, strides, box,
                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -414,10 +426,14 @@ int make_token_map(CUtensorMap* map, const void* base, long long rows, int inner
 
 using namespace musc;
 
-extern "C" int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* out, int batch,
-                                       int tokens, int heads, int head_dim, long long qkv_row_stride,
-                                       long long out_row_stride, float scale, musc_b200_stream stream) {
+extern "C" int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* out, int dtype,
+                                       int batch, int tokens, int heads, int head_dim,
+                                       long long qkv_row_stride, long long out_row_stride, float scale,
+                                       musc_b200_stream stream) {
   if (!q || !k || !v || !out) return fail(MUSC_B200_ERR_INVALID, "attention: null pointer");
+  if (dtype != MUSC_B200_F16 && dtype != MUSC_B200_BF16)
+    return fail(MUSC_B200_ERR_INVALID, "attention: dtype must be f16 or bf16");
+  const bool fp16 = dtype == MUSC_B200_F16;
   if (batch <= 0 || tokens <= 0 || heads <= 0)
     return fail(MUSC_B200_ERR_INVALID, "attention: batch, tokens and heads must be positive");
   if (head_dim != attn::D) return fail(MUSC_B200_ERR_INVALID, "attention: head_dim must be 64");
@@ -432,11 +448,11 @@ extern "C" int musc_b200_attention_fwd(const void* q, const void* k, const void*
   MUSC_TRY(require_sm100());
   const int inner = heads * head_dim;
   CUtensorMap mq, mk, mv;
-  MUSC_TRY(make_token_map(&mq, q, rows, inner, qkv_row_stride));
-  MUSC_TRY(make_token_map(&mk, k, rows, inner, qkv_row_stride));
-  MUSC_TRY(make_token_map(&mv, v, rows, inner, qkv_row_stride));
+  MUSC_TRY(make_token_map(&mq, q, rows, inner, qkv_row_stride, fp16));
+  MUSC_TRY(make_token_map(&mk, k, rows, inner, qkv_row_stride, fp16));
+  MUSC_TRY(make_token_map(&mv, v, rows, inner, qkv_row_stride, fp16));
   attn::Params p;
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out = out;
   p.out_row_stride = out_row_stride;
   p.err = device_error_ptr();
   if (!p.err) return fail(MUSC_B200_ERR_CUDA, "attention: device error word unavailable");
@@ -452,14 +468,19 @@ extern "C" int musc_b200_attention_fwd(const void* q, const void* k, const void*
   {
     std::lock_guard<std::mutex> lock(m);
     if (dev >= 64 || !attr_done[dev]) {
-      MUSC_CUDA(cudaFuncSetAttribute(attn::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      MUSC_CUDA(cudaFuncSetAttribute(attn::attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)attn::SMEM_BYTES));
+      MUSC_CUDA(cudaFuncSetAttribute(attn::attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)attn::SMEM_BYTES));
       if (dev < 64) attr_done[dev] = true;
     }
   }
   const long long grid = (long long)batch * heads * p.n_q_tiles;
   if (grid > 0x7FFFFFFFLL) return fail(MUSC_B200_ERR_INVALID, "attention: grid too large");
-  attn::attention_kernel<<<(unsigned)grid, attn::THREADS, attn::SMEM_BYTES,
-                           reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, p);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (fp16)
+    attn::attention_kernel<true><<<(unsigned)grid, attn::THREADS, attn::SMEM_BYTES, s>>>(mq, mk, mv, p);
+  else
+    attn::attention_kernel<false><<<(unsigned)grid, attn::THREADS, attn::SMEM_BYTES, s>>>(mq, mk, mv, p);
   return check_launch("attention_kernel");
 }

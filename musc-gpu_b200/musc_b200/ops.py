@@ -253,14 +253,14 @@ def score_maps(scores: torch.Tensor, image_size: int = 518, upsampled: bool = Fa
 # --------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
-    """``softmax(q k^T * scale) v`` per head for token-major bf16 ``(B, L, heads*64)`` views.
+    """``softmax(q k^T * scale) v`` per head for token-major ``(B, L, heads*64)`` views.
 
-    ``q``, ``k``, ``v`` may be column slices of one packed QKV projection (same row
-    stride); the result is ``(B, L, heads*64)`` bf16.
+    ``q``, ``k``, ``v`` (fp16 or bf16, one type) may be column slices of one packed QKV
+    projection (same row stride); the result is ``(B, L, heads*64)`` in that type.
     """
     _require_cuda(q, 'attention')
-    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
-        raise ValueError('attention: q, k, v must be bfloat16')
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError('attention: q, k, v must all be float16 or all bfloat16')
     if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape:
         raise ValueError('attention: q, k, v must share shape (B, L, heads*head_dim)')
     b, length, width = q.shape
@@ -271,11 +271,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, sca
         if t.stride(2) != 1 or t.stride(0) != length * t.stride(1) or t.stride(1) != q.stride(1):
             raise ValueError('attention: q, k, v must be token-major with one common row stride')
     if out is None:
-        out = torch.empty(b, length, width, dtype=torch.bfloat16, device=q.device)
+        out = torch.empty(b, length, width, dtype=q.dtype, device=q.device)
     scale = head_dim ** -0.5 if scale is None else scale
     dev = q.device
     with torch.cuda.device(dev):
-        st = _lib.lib().musc_b200_attention_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, length, heads,
+        st = _lib.lib().musc_b200_attention_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _DTYPES[q.dtype], b,
+                                                length, heads,
                                                 head_dim, q.stride(1), out.stride(1), float(scale),
                                                 _stream(dev))
         _lib.check(st, 'musc_b200_attention_fwd')

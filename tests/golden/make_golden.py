@@ -8,11 +8,14 @@ available (it is read only through ``--reference``)::
 The script imports the reference's ``original`` modules --
 ``models/modules/_MSM.py`` (``MSM``), ``models/modules/_LNAMD.py``
 (``LNAMD._embed``), ``models/modules/_encoder_gpu.py``
-(``aggregate_features``) and ``models/modules/_super_fast.py``
-(``SuperFastAggregation``) -- and evaluates the score reduction of
-``models/musc.py:259-288`` with the same torch calls.  Inputs are either stored
-in the fixture (small cases) or regenerated from ``musc_b200.synthetic`` with
-the recorded seed (the N=16 prototype-mixture pool).  Nothing at test time reads
+(``aggregate_features``), ``models/modules/_super_fast.py``
+(``SuperFastAggregation``) and the CLIP ``VisionTransformer``
+(``models/backbone/open_clip/transformer.py``) -- and evaluates the score
+reduction of ``models/musc.py:259-288`` with the same torch calls.  Inputs are
+either stored in the fixture (small cases) or regenerated with the recorded
+seed (the N=16 prototype-mixture pool from ``musc_b200.synthetic``; the
+encoder pool's images and random ViT-L/14 weights from
+``musc_b200.synthetic.random_images`` and ``musc_b200.encoder.random_vit_state``).  Nothing at test time reads
 the reference; the tests read only the ``.npz`` files written here.
 """
 from __future__ import annotations
@@ -132,6 +135,60 @@ def make_pool16(MSM, LNAMD, encoder_gpu) -> dict:
             'bank_probe': bank_probe}
 
 
+def _reference_vit_class(reference: str):
+    """The reference's ``VisionTransformer`` (``models/backbone/open_clip/transformer.py``),
+    imported under a stub package so ``open_clip/__init__.py`` (tokenizer, ftfy) is skipped."""
+    import importlib
+    import types
+    name = 'reference_open_clip'
+    if name not in sys.modules:
+        pkg = types.ModuleType(name)
+        pkg.__path__ = [os.path.join(reference, 'models', 'backbone', 'open_clip')]
+        sys.modules[name] = pkg
+    return importlib.import_module(name + '.transformer').VisionTransformer
+
+
+def make_encoder_pool(MSM, LNAMD, reference: str) -> dict:
+    """Config 5 in miniature: the reference ViT-L/14 (fp32, CPU) on 6 seeded images with
+    seeded random weights, hooks after blocks 6/12/18/24, then LNAMD r{1,3,5} + MSM +
+    the score reduction -- the whole reference pipeline from pixels to image scores."""
+    from musc_b200.encoder import random_vit_state
+    from musc_b200.synthetic import random_images
+    VisionTransformer = _reference_vit_class(reference)
+    torch.set_num_threads(os.cpu_count() or 1)
+    n, seed = 6, 5
+    vit = VisionTransformer(image_size=518, patch_size=14, width=1024, layers=24, heads=16, mlp_ratio=4.0,
+                            output_dim=768)
+    vit.load_state_dict(random_vit_state(seed), strict=True)
+    vit.eval()
+    images = random_images(n, 518, seed=seed)
+    out_layers = [6, 12, 18, 24]
+    tokens = [[] for _ in out_layers]
+    pooled = []
+    with torch.no_grad():
+        for i in range(n):
+            pl, toks = vit(images[i:i + 1], out_layers)
+            pooled.append(pl)
+            for li, t in enumerate(toks):
+                tokens[li].append(t)
+    tokens = [torch.cat(t) for t in tokens]
+    probe = np.arange(0, 1370, 17)
+    radii = (1, 3, 5)
+    scores = torch.empty(len(radii), 4, n, 1369, dtype=torch.float64)
+    for ri, r in enumerate(radii):
+        lnamd = LNAMD(device='cpu', r=r, feature_dim=1024, feature_layer=[1, 2, 3, 4])
+        feats = lnamd._embed(tokens, return_cpu=True)
+        feats /= feats.norm(dim=-1, keepdim=True)
+        for li in range(4):
+            scores[ri, li] = MSM(feats[:, :, li, :].contiguous(), 'cpu', topmin_min=0, topmin_max=0.3)
+    maps, image_max, _ = _reduce_like_musc(scores, 518)
+    return {'seed': np.array(seed), 'n': np.array(n), 'out_layers': np.array(out_layers),
+            'pooled': torch.cat(pooled).numpy(), 'token_probe_rows': probe,
+            'tokens_probe': np.stack([t[:, probe].numpy() for t in tokens]),
+            'token_rms': np.array([float(t.pow(2).mean().sqrt()) for t in tokens]),
+            'scores': scores.numpy(), 'maps': maps, 'image_max': image_max}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True)
@@ -142,7 +199,8 @@ def main() -> None:
     jobs = {'msm_small': lambda: make_msm_small(MSM),
             'lnamd_small': lambda: make_lnamd_small(LNAMD, encoder_gpu, super_fast),
             'reduce_small': make_reduce_small,
-            'pool16': lambda: make_pool16(MSM, LNAMD, encoder_gpu)}
+            'pool16': lambda: make_pool16(MSM, LNAMD, encoder_gpu),
+            'encoder_pool6': lambda: make_encoder_pool(MSM, LNAMD, args.reference)}
     for name, job in jobs.items():
         if args.only and name not in args.only.split(','):
             continue

@@ -2,7 +2,8 @@
 
 Reference: a plain PyTorch fp32 evaluation of ``softmax(q k^T * scale) v`` on the same bf16
 inputs (and the numpy oracle for one small case).  Tolerance: the kernel rounds P and the
-output to bf16 (2^-9 relative), so outputs are compared at 1e-2 relative + 2e-3 absolute.
+output to the 16-bit input type (bf16: 2^-9 relative), so outputs are compared at 1e-2
+relative + 2e-3 absolute.
 """
 from __future__ import annotations
 
@@ -21,13 +22,14 @@ def _ref(q, k, v, heads, scale):
     return (p @ vf).transpose(1, 2).reshape(b, length, width)
 
 
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize('b,length,heads', [(2, 200, 2), (1, 1, 1), (3, 128, 1), (1, 129, 3),
                                             (2, 1370, 16)])
-def test_attention_matches_fp32_reference(cuda_device, b, length, heads):
+def test_attention_matches_fp32_reference(cuda_device, b, length, heads, dtype):
     from musc_b200 import ops
     g = torch.Generator(device=cuda_device).manual_seed(b * 1000 + length + heads)
     width = heads * 64
-    qkv = torch.randn(b, length, 3 * width, generator=g, device=cuda_device).to(torch.bfloat16)
+    qkv = torch.randn(b, length, 3 * width, generator=g, device=cuda_device).to(dtype)
     q, k, v = qkv[..., :width], qkv[..., width:2 * width], qkv[..., 2 * width:]
     out = ops.attention(q, k, v, heads)
     want = _ref(q, k, v, heads, 64 ** -0.5)
