@@ -56,7 +56,10 @@ def _args():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--pool', type=int, default=N_POOL)
+    ap.add_argument('--pool', type=int, default=None, help='pool size (default: the config\'s)')
+    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5'],
+                    help='BASELINE.json config: 2 (default, the metric\'s), 3 super-fast, 4 N=1024, '
+                         '5 encoder end to end')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     return ap.parse_args()
 
@@ -179,7 +182,8 @@ def run_reference(args):
         return
     sys.path.insert(0, str(REPO))
     cores = os.cpu_count() or 1
-    sample = CpuSample(args.pool)
+    pool = args.pool if args.pool is not None else N_POOL
+    sample = CpuSample(pool)
     for _ in range(max(args.warmup, 0)):
         sample.per_image_seconds()
     times = [sample.per_image_seconds() for _ in range(args.steps)]
@@ -187,11 +191,11 @@ def run_reference(args):
     value = 1.0 / per_image
     line = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
-        'warmup': args.warmup, 'ms_per_step': per_image * args.pool * 1e3, 'higher_is_better': True,
+        'warmup': args.warmup, 'ms_per_step': per_image * pool * 1e3, 'higher_is_better': True,
         'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
         'impl': 'reference',
-        'config': {'workload': f'config2: pool N={args.pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32',
-                   'global_batch': args.pool, 'l2': 'inputs larger than L2'},
+        'config': {'workload': f'config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32',
+                   'global_batch': pool, 'l2': 'inputs larger than L2'},
         'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
                          'sample': CPU_SAMPLE_TEXT},
         'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
@@ -213,12 +217,29 @@ def symmetric_tiles(rows: int, patches: int, n_images: int, bm: int = 128, bn: i
 
 
 # ----------------------------------------------------------------- GPU arm
+CONFIGS = {
+    '2': dict(pool=100, layers=4, radii=(1, 3, 5), super_fast=None, encoder=False,
+              desc='config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 prototype-mixture '
+                   'tokens resident in HBM'),
+    '3': dict(pool=100, layers=1, radii=(3,), super_fast=28, encoder=False,
+              desc='config3 super-fast: pool N={pool}, 1 layer, r=3 then 37x37->28x28 (784 patches), '
+                   'C=1024 fp32 prototype-mixture tokens'),
+    '4': dict(pool=1024, layers=4, radii=(1, 3, 5), super_fast=None, encoder=False,
+              desc='config4: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 prototype-mixture tokens'),
+    '5': dict(pool=200, layers=4, radii=(1, 3, 5), super_fast=None, encoder=True,
+              desc='config5 end to end: random-init ViT-L/14 (24 blocks, d=1024, 16x64 heads, fp16 GEMMs + '
+                   'fused attention) on N={pool} seeded 518x518x3 U[0,1] images, batch 4, hooks 6/12/18/24, '
+                   'then LNAMD r{{1,3,5}} + MSM + reduction'),
+}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
     from musc_b200 import ops, pipeline
-    from musc_b200.synthetic import prototype_mixture
+    from musc_b200.synthetic import prototype_mixture, random_images
 
+    cfg = CONFIGS[args.config]
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local_rank = int(os.environ.get('LOCAL_RANK', '0'))
@@ -229,46 +250,85 @@ def run_b200(args):
     group = None
     if world > 1:
         import datetime
-        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=300))
         group = dist.group.WORLD
 
-    pool = args.pool
+    pool = args.pool if args.pool is not None else cfg['pool']
+    radii, n_layers, sf = cfg['radii'], cfg['layers'], cfg['super_fast']
+    p_score = sf * sf if sf else P
     first, end, _ = pipeline.shard_range(pool, world, rank)
-    host = [t[first:end].contiguous().pin_memory() for t in prototype_mixture(pool, N_LAYERS, C, SIDE, seed=0)]
-    tokens = [h.to(dev, non_blocking=True) for h in host]
+    n_local = end - first
+
+    # ---- inputs: pinned host copies + resident device copies of this rank's images
+    encoder = None
+    if cfg['encoder']:
+        from musc_b200.encoder import VisionEncoder, random_vit_state
+        encoder = VisionEncoder(random_vit_state(0), device=dev)
+        host = [random_images(pool, 518, seed=0)[first:end].contiguous().pin_memory()]
+    else:
+        host = [t[first:end].contiguous().pin_memory()
+                for t in prototype_mixture(pool, n_layers, C, SIDE, seed=0)]
+    resident = [h.to(dev, non_blocking=True) for h in host]
     torch.cuda.synchronize()
+    h2d = sum(h.numel() * h.element_size() for h in host)
 
-    # Instrument the dominant kernel's launches with events on its stream.
-    near_events = []
-    orig_nearest = ops.nearest_pool
-
-    def timed_nearest(*a, **k):
-        s = torch.cuda.current_stream(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        out = orig_nearest(*a, **k)
-        e1.record(s)
-        near_events.append((e0, e1))
-        return out
+    # ---- our kernels, instrumented: launch counts and the dominant kernel's event timing
+    near_events, launches = [], [0]
+    per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'prep_bank': 1, 'nearest_pool': 2, 'trimmed_mean': 1,
+                'score_maps': 1}
 
     class Kernels:
-        pass
+        trimmed_ranks = staticmethod(ops.trimmed_ranks)
     kern = Kernels()
-    for name in ('lnamd', 'lnamd_super_fast', 'prep_bank', 'trimmed_mean', 'score_maps', 'trimmed_ranks'):
-        setattr(kern, name, getattr(ops, name))
-    kern.nearest_pool = timed_nearest
 
-    def step():
-        return pipeline.score_pool(tokens, n_images=pool, radii=RADII, group=group, kernels=kern)
+    def counted(name):
+        fn = getattr(ops, name)
+
+        def call(*a, **k):
+            launches[0] += per_call[name]
+            if name != 'nearest_pool':
+                return fn(*a, **k)
+            st = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            out = fn(*a, **k)
+            e1.record(st)
+            near_events.append((e0, e1))
+            return out
+        return call
+    for name in per_call:
+        setattr(kern, name, counted(name))
+    orig_attention = ops.attention
+
+    def counted_attention(*a, **k):
+        launches[0] += 1
+        return orig_attention(*a, **k)
+    ops.attention = counted_attention
+
+    def tokens_of(inputs):
+        if encoder is None:
+            return inputs
+        images = inputs[0]
+        layers = [[] for _ in range(4)]
+        for i in range(0, images.shape[0], 4):           # the reference's batch size
+            _, toks = encoder.forward(images[i:i + 4], [6, 12, 18, 24])
+            for li, t in enumerate(toks):
+                layers[li].append(t)
+        return [torch.cat(t) if t else torch.empty(0, 1 + P, C, device=dev) for t in layers]
+
+    def step(inputs, ready=None):
+        return pipeline.score_pool(tokens_of(inputs), n_images=pool, radii=radii, group=group, kernels=kern,
+                                   super_fast_side=sf, ready=None if encoder is not None else ready)
 
     def barrier():
         if group is not None:
             dist.barrier(device_ids=[local_rank])
 
     for _ in range(args.warmup):
-        step()
+        step(resident)
     torch.cuda.synchronize()
     near_events.clear()
+    launches[0] = 0
     barrier()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
@@ -276,21 +336,31 @@ def run_b200(args):
     with ClockSampler(local_rank) as clocks:
         t0.record(stream)
         for _ in range(args.steps):
-            step()
+            step(resident)
         t1.record(stream)
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = t0.elapsed_time(t1)
     near_ms = [a.elapsed_time(b) for a, b in near_events]
+    launches_timed = launches[0]
 
-    # e2e: host tokens in, maps and image maxima out, every step.
-    dev_buf = [torch.empty_like(t) for t in tokens]
-    h2d = sum(h.numel() * h.element_size() for h in host)
+    # ---- e2e: pinned host inputs in (per-layer copies on a side stream, each layer's
+    # scoring waits only for its own copy), maps and image maxima out, every step.
+    dev_buf = [torch.empty_like(t) for t in resident]
+    copy_stream = torch.cuda.Stream(dev)
 
     def e2e_step():
-        for h, d in zip(host, dev_buf):
-            d.copy_(h, non_blocking=True)
-        res = pipeline.score_pool(dev_buf, n_images=pool, radii=RADII, group=group)
+        events = []
+        copy_stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(copy_stream):
+            for h, d in zip(host, dev_buf):
+                d.copy_(h, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                events.append(ev)
+        if encoder is not None:
+            torch.cuda.current_stream(dev).wait_event(events[-1])
+        res = step(dev_buf, ready=events)
         maps, mx = pipeline.gather_pool(res, group)
         if rank == 0:
             return maps.cpu(), mx.cpu()
@@ -310,6 +380,7 @@ def run_b200(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
+    ops.attention = orig_attention
 
     stats = torch.tensor([elapsed_ms, e2e_ms, sum(near_ms) / max(len(near_ms), 1)], dtype=torch.float64,
                          device=dev)
@@ -321,37 +392,37 @@ def run_b200(args):
         peaks, peak_kind = _peaks()
         ms_per_step = elapsed_ms / args.steps
         value = pool / (ms_per_step / 1e3)
-        n_local = end - first
-        # algorithmic (directed) MSM flops per bank: 2*C*P^2*N*(N-1), this rank's share
-        msm_flop_per_bank = 2.0 * C * P * P * pool * (pool - 1)
-        achieved_tflops = msm_flop_per_bank * (n_local / pool) / (near_avg_ms / 1e3) / 1e12
+        # algorithmic (directed) MSM flops per bank, 2*C*P^2*N*(N-1) (the count the reference's
+        # original path computes); each rank's launch covers 1/world of the pool's tiles
+        msm_flop_per_bank = 2.0 * C * p_score * p_score * pool * (pool - 1)
+        achieved_tflops = msm_flop_per_bank / world / (near_avg_ms / 1e3) / 1e12
         # executed tensor-core work: 3 MMA passes over the symmetric tiles (whole 128 x 256
         # tiles holding a pair of different images, each pair once), this rank's share
-        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * P, P, pool) * 128 * 256 * C / world
+        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * p_score, p_score, pool) * 128 * 256 * C / world
                       / (near_avg_ms / 1e3) / 1e12)
         peak = peaks.get('bf16_tflops_sustained', peaks.get('bf16_tflops'))
-        launches_per_step = N_LAYERS * 2 + len(RADII) * N_LAYERS * 4 + 1
         line = {
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
             'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-            'config': {'workload': f'config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 '
-                                   'prototype-mixture tokens resident in HBM',
-                       'global_batch': pool, 'seq_len': P, 'parallelism': f'query-shard{world}',
-                       'l2': f'inputs larger than L2 ({h2d * world / 1e9:.2f} GB tokens per step); no flush'},
+            'config': {'workload': cfg['desc'].format(pool=pool), 'global_batch': pool, 'seq_len': p_score,
+                       'parallelism': f'query-shard{world}',
+                       'l2': f'inputs larger than L2 ({h2d * world / 1e9:.2f} GB per step); no flush'},
             'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
                     'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
             'roofline': {'kernel': 'nearest_kernel', 'bound': 'tensor', 'achieved': achieved_tflops,
                          'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved_tflops / peak,
-                         'traffic': _traffic(),
+                         'traffic': _traffic() if (args.config == '2' and pool == N_POOL) else None,
                          'peak_kind': f'{peak_kind} bf16 sustained (kernel timed inside a long step)',
                          'mma_executed_tflops': mma_tflops, 'mma_frac': mma_tflops / peak,
                          'mma_kind': 'kind::f16 (fp16 split hi/lo, 3 passes, symmetric tiles)',
                          'launch_ms': near_avg_ms},
-            'gpu_launches': launches_per_step * args.steps,
+            'gpu_launches': launches_timed,
             'clocks': clocks.summary(),
         }
-        if not args.no_cpu_baseline:
+        if args.config == '5':
+            line['dtype'] = 'f32 scoring, fp16 encoder'
+        if not args.no_cpu_baseline and args.config == '2':
             sys.path.insert(0, str(REPO))
             sample = CpuSample(pool)
             sample.per_image_seconds()

@@ -55,7 +55,7 @@ class PoolScores:
 def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
                radii: Sequence[int] = (1, 3, 5), topmin_min: float = 0, topmin_max: float = 0.3,
                image_size: int = 518, super_fast_side: int | None = None,
-               group=None, kernels=ops) -> PoolScores:
+               group=None, kernels=ops, ready: Sequence | None = None) -> PoolScores:
     """Score one pool from device-resident tokens.
 
     ``tokens``: per hooked layer, this rank's ``(n_local, 1+P, C)`` tokens
@@ -64,6 +64,10 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     ``group``: a ``torch.distributed`` process group (None = single GPU).
     ``kernels``: the operator set (``musc_b200.ops``, the CUDA library); the
     CPU tests of the sharding logic substitute the numpy oracle here.
+    ``ready``: optional per-layer CUDA events (e.g. the end of each layer's
+    host-to-device copy on another stream); the current stream waits on layer
+    l's event just before that layer's LNAMD, so later layers' copies overlap
+    the scoring of earlier ones.  Banks are processed layer by layer.
     """
     import torch.distributed as dist
 
@@ -88,14 +92,25 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     side = math.isqrt(p)
     n_r, n_l = len(radii), len(tokens)
 
-    # 1. LNAMD of the local images into (R*L) local banks, padded to `per` images.
-    local = torch.zeros(n_l, n_r, per, p, c, dtype=torch.float32, device=dev)
-    for li, t in enumerate(tokens):
+    # 1. LNAMD of the local images into (R*L) local banks, padded to `per` images
+    #    (only the padding is zeroed: it is gathered but never scored).
+    local = torch.empty(n_l, n_r, per, p, c, dtype=torch.float32, device=dev)
+    if per > n_local:
+        local[:, :, n_local:].zero_()
+    done = [False] * n_l
+
+    def aggregate(li: int) -> None:
+        if done[li]:
+            return
+        done[li] = True
+        if ready is not None and ready[li] is not None and dev.type == 'cuda':
+            torch.cuda.current_stream(dev).wait_event(ready[li])
         if n_local == 0:
-            continue
+            return
+        t = tokens[li]
         if super_fast_side is not None:
             kernels.lnamd_super_fast(t, super_fast_side, True, out=local[li, 0, :n_local],
-                                 image_stride=p * c, patch_stride=c)
+                                     image_stride=p * c, patch_stride=c)
         else:
             kernels.lnamd(t, radii, True, out=[local[li, ri, :n_local] for ri in range(n_r)])
 
@@ -103,7 +118,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     #    Rank r evaluates part r of the pool's symmetric tile list into a table
     #    whose blocks are the ranks' query rows; a MIN reduce-scatter hands each
     #    rank the minima of its own rows.
-    banks = [(li, ri) for ri in range(n_r) for li in range(n_l)]
+    banks = [(li, ri) for li in range(n_l) for ri in range(n_r)]
     scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
     rows = n_images * p
     q_rows = n_local * p
@@ -114,16 +129,19 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     if world > 1:
         full = [torch.empty(world * per, p, c, dtype=torch.float32, device=dev) for _ in range(2)]
         works = [None] * len(banks)
+        aggregate(banks[0][0])
         works[0] = dist.all_gather_into_tensor(full[0], local[banks[0]], group=group, async_op=True)
     for k, (li, ri) in enumerate(banks):
         if world > 1:
             if k + 1 < len(banks):
                 nxt = banks[k + 1]
+                aggregate(nxt[0])
                 works[k + 1] = dist.all_gather_into_tensor(full[(k + 1) % 2], local[nxt], group=group,
                                                            async_op=True)
             works[k].wait()
             z_full = full[k % 2][:n_images]
         else:
+            aggregate(li)
             z_full = local[li, ri, :n_images]
         bank = kernels.prep_bank(z_full.reshape(rows, c))
         kernels.nearest_pool(bank, rows, c, p, rank, world, rpb, out=table)
