@@ -237,7 +237,7 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
     from musc_b200 import ops, pipeline
-    from musc_b200.synthetic import prototype_mixture, random_images
+    from musc_b200.synthetic import prototype_mixture_images, random_images
 
     cfg = CONFIGS[args.config]
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -264,10 +264,11 @@ def run_b200(args):
     if cfg['encoder']:
         from musc_b200.encoder import VisionEncoder, random_vit_state
         encoder = VisionEncoder(random_vit_state(0), device=dev)
-        host = [random_images(pool, 518, seed=0)[first:end].contiguous().pin_memory()]
+        host = [random_images(end, 518, seed=0)[first:end].contiguous().pin_memory()]
     else:
-        host = [t[first:end].contiguous().pin_memory()
-                for t in prototype_mixture(pool, n_layers, C, SIDE, seed=0)]
+        # this rank's images only, generated on its GPU (per-image seeds: shard-independent)
+        host = [t.cpu().pin_memory()
+                for t in prototype_mixture_images(range(first, end), n_layers, C, SIDE, seed=0, device=dev)]
     resident = [h.to(dev, non_blocking=True) for h in host]
     torch.cuda.synchronize()
     h2d = sum(h.numel() * h.element_size() for h in host)
@@ -279,6 +280,7 @@ def run_b200(args):
 
     class Kernels:
         trimmed_ranks = staticmethod(ops.trimmed_ranks)
+        nearest_pool_table = staticmethod(ops.nearest_pool_table)
     kern = Kernels()
 
     def counted(name):

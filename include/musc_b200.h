@@ -153,7 +153,11 @@ int musc_b200_nearest(const void* query_bank, long long query_rows, long long qu
  * element-wise MIN reduction of the tables).
  * Layout: nearest_sq[block][image][r], block = row / rows_per_block,
  * r = row % rows_per_block, n_images = rows / patches_per_image; the call
- * first fills the whole table (musc_b200_nearest_pool_bytes) with FLT_MAX.
+ * first fills the whole table with FLT_MAX.  The buffer must hold
+ * musc_b200_nearest_pool_bytes: the table plus a 256-byte word after it (at
+ * the table size rounded up to 256 bytes) that the kernel's dynamic tile
+ * scheduler uses; CTAs claim tiles from it, so ones that start late take
+ * fewer.
  * rows_per_block = rows gives the plain [image][row] table;
  * rows_per_block = one rank's rows makes each rank's rows contiguous for a
  * reduce-scatter. */

@@ -112,6 +112,8 @@ constexpr int GROUP_M = 64;  // m-tiles swept together over the reference column
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;  // 4 s per wait
 constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, /*fp16*/ 0);
 constexpr float INF = FLT_MAX;
+constexpr int RING = 8;      // tile indices handed from the producer to the MMA and epilogue warps
+constexpr int CHUNK = 8;     // tiles claimed per atomic by the dynamic scheduler
 
 struct Smem {
   uint8_t tiles[STAGES][STAGE_BYTES];  // 1024-aligned base
@@ -122,6 +124,9 @@ struct Smem {
   uint64_t acc_full[NUM_ACC];
   uint64_t acc_empty[NUM_ACC];
   uint64_t drain;
+  uint64_t ring_full[RING];
+  uint64_t ring_empty[RING];
+  long long tile_ring[RING];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -133,6 +138,7 @@ struct Params {
   const float* r_norm;
   const float* r_inv;
   unsigned int* nearest;  // float bits, layout [row / rpb][image][row % rpb]
+  unsigned long long* sched;  // dynamic-scheduler counter (zeroed before the launch), or nullptr
   int* err;
   long long q_rows, r_rows, q_first_row;
   long long tile_begin, tile_end;  // linear tile range processed by this launch
@@ -254,6 +260,10 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       tc::mbar_init(tc::smem_u32(&sm.acc_empty[a]), EPI_WARPS);
     }
     tc::mbar_init(tc::smem_u32(&sm.drain), 1);
+    for (int i = 0; i < RING; ++i) {
+      tc::mbar_init(tc::smem_u32(&sm.ring_full[i]), 1);
+      tc::mbar_init(tc::smem_u32(&sm.ring_empty[i]), EPI_WARPS);
+    }
     sm.abort_flag = 0;
     tc::fence_barrier_init();
     tc::prefetch_tensormap(&map_q_hi);
@@ -279,10 +289,45 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end && ok; tile += gridDim.x) {
+      long long next_static = p.tile_begin + blockIdx.x, chunk_cur = 0, chunk_end = 0;
+      // Next tile this CTA evaluates (linear index), or -1.  Static: stride gridDim.x.
+      // Dynamic: claim CHUNK consecutive indices per atomic, so CTAs that start late
+      // (their SM busy with another kernel, e.g. a collective) simply take fewer.
+      auto next_tile = [&]() -> long long {
+        while (true) {
+          long long t;
+          if (p.sched) {
+            if (chunk_cur >= chunk_end) {
+              const long long c = (long long)atomicAdd(p.sched, 1ull);
+              chunk_cur = p.tile_begin + c * CHUNK;
+              chunk_end = chunk_cur + CHUNK < p.tile_end ? chunk_cur + CHUNK : p.tile_end;
+              if (chunk_cur >= p.tile_end) return -1;
+            }
+            t = chunk_cur++;
+          } else {
+            t = next_static;
+            if (t >= p.tile_end) return -1;
+            next_static += gridDim.x;
+          }
+          if (!SYM) return t;
+          int mb, nb;
+          tile_coords(t, p.num_m, p.num_n, &mb, &nb);
+          if (sym_needed(mb, nb, p.r_rows, p.patches, p.n_images)) return t;
+        }
+      };
+      for (int local = 0; ok; ++local) {
+        const int slot = local % RING;
+        if (!wait_bounded(tc::smem_u32(&sm.ring_empty[slot]), ((uint32_t)(local / RING) & 1u) ^ 1u,
+                          abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        const long long tile = next_tile();
+        sm.tile_ring[slot] = tile;
+        tc::mbar_arrive(tc::smem_u32(&sm.ring_full[slot]));
+        if (tile < 0) break;
         int m_blk, n_blk;
         tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
-        if (SYM && !sym_needed(m_blk, n_blk, p.r_rows, p.patches, p.n_images)) continue;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!wait_bounded(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err)) {
             ok = false;
@@ -320,12 +365,14 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end && ok; tile += gridDim.x) {
-        if (SYM) {
-          int m_blk, n_blk;
-          tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
-          if (!sym_needed(m_blk, n_blk, p.r_rows, p.patches, p.n_images)) continue;
+      for (int local = 0; ok; ++local) {
+        const int slot = local % RING;
+        if (!wait_bounded(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u, abort_flag,
+                          p.err)) {
+          ok = false;
+          break;
         }
+        if (sm.tile_ring[slot] < 0) break;
         if (!wait_bounded(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err)) {
           ok = false;
           break;
@@ -372,10 +419,14 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
     const int P = p.patches;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (long long tile = p.tile_begin + blockIdx.x; tile < p.tile_end; tile += gridDim.x) {
+    for (int local = 0;; ++local) {
+      const int slot = local % RING;
+      const bool got = wait_bounded(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u,
+                                    abort_flag, p.err);
+      const long long tile = got ? sm.tile_ring[slot] : -1;
+      if (named_sync_epi_any(tile < 0)) break;  // uniform: every epilogue thread read the same slot
       int m_blk, n_blk;
       tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
-      if (SYM && !sym_needed(m_blk, n_blk, p.r_rows, P, p.n_images)) continue;
       const long long n0 = (long long)n_blk * BN;
       named_sync_epi();  // previous tile's readers are done with col_norm / col_w
       for (int j = et; j < BN; j += EPI_WARPS * 32) {
@@ -470,7 +521,10 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       if (row_ok && seg_img != q_img) flush_min(p, row, seg_img, m);
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.acc_empty[acc]));
+      if (lane == 0) {
+        tc::mbar_arrive(tc::smem_u32(&sm.acc_empty[acc]));
+        tc::mbar_arrive(tc::smem_u32(&sm.ring_empty[slot]));
+      }
       if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
     }
   }
@@ -710,6 +764,7 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   p.num_n = (int)((ref_rows + nearest::BN - 1) / nearest::BN);
   p.tile_begin = 0;
   p.tile_end = (long long)p.num_m * p.num_n;
+  p.sched = nullptr;  // static schedule
   MUSC_TRY(set_smem_attr());
   const int grid = (int)std::min<long long>(p.tile_end, sm_count());
   nearest::nearest_kernel<false><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mqh, mql, mrh, mrl, p);
@@ -727,11 +782,17 @@ int nearest_pool_launch(const void* bank, long long rows, int channels, int patc
   MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, nearest::BN));
   const int n_images = (int)(rows / patches);
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  MUSC_TRY(fill_table(nearest_sq, blocks * n_images * rows_per_block, s));
+  const long long table = blocks * n_images * rows_per_block;
+  MUSC_TRY(fill_table(nearest_sq, table, s));
+  // The scheduler counter lives in the 256 bytes after the table (musc_b200_nearest_pool_bytes).
+  unsigned long long* sched = reinterpret_cast<unsigned long long*>(
+      reinterpret_cast<uint8_t*>(nearest_sq) + ((size_t)table * sizeof(float) + 255) / 256 * 256);
+  MUSC_CUDA(cudaMemsetAsync(sched, 0, sizeof(unsigned long long), s));
   nearest::Params p;
   p.q_norm = p.r_norm = reinterpret_cast<const float*>(b + l.norm);
   p.q_inv = p.r_inv = reinterpret_cast<const float*>(b + l.inv);
   p.nearest = reinterpret_cast<unsigned int*>(nearest_sq);
+  p.sched = sched;
   p.err = device_error_ptr();
   if (!p.err) return fail(MUSC_B200_ERR_CUDA, "nearest_pool: device error word unavailable");
   p.q_rows = p.r_rows = rows;
@@ -746,7 +807,7 @@ int nearest_pool_launch(const void* bank, long long rows, int channels, int patc
   sym_part_range(rows, patches, n_images, p.num_m, p.num_n, part, parts, &p.tile_begin, &p.tile_end);
   if (p.tile_end <= p.tile_begin) return MUSC_B200_OK;  // nothing to do for this part
   MUSC_TRY(set_smem_attr());
-  const int grid = (int)std::min<long long>(p.tile_end - p.tile_begin, sm_count());
+  const int grid = sm_count();
   nearest::nearest_kernel<true><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mah, mal, mbh, mbl, p);
   return check_launch("nearest_kernel<symmetric>");
 }
@@ -813,7 +874,8 @@ extern "C" size_t musc_b200_nearest_pool_bytes(long long rows, int patches_per_i
                                                long long rows_per_block) {
   if (rows <= 0 || patches_per_image <= 0 || rows_per_block <= 0) return 0;
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  return (size_t)blocks * (size_t)(rows / patches_per_image) * (size_t)rows_per_block * sizeof(float);
+  const size_t table = (size_t)blocks * (size_t)(rows / patches_per_image) * (size_t)rows_per_block * sizeof(float);
+  return (table + 255) / 256 * 256 + 256;  // + the dynamic scheduler's counter
 }
 
 extern "C" int musc_b200_nearest_pool(const void* bank, long long rows, int channels, int patches_per_image,
@@ -852,7 +914,7 @@ extern "C" int musc_b200_trimmed_mean(const float* nearest_sq, long long query_r
 extern "C" size_t musc_b200_msm_workspace_bytes(int n, int p, int c) {
   if (n <= 0 || p <= 0 || c <= 0) return 0;
   const long long rows = (long long)n * p;
-  return bank_layout(rows, c).total + align_up((size_t)rows * n * 4, 1024);
+  return bank_layout(rows, c).total + align_up(musc_b200_nearest_pool_bytes(rows, p, rows), 1024);
 }
 
 extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi, double* scores,

@@ -169,6 +169,20 @@ def nearest(query_bank: torch.Tensor, query_rows: int, query_first_row: int, ref
     return out
 
 
+def nearest_pool_table(rows: int, patches: int, rows_per_block: int | None = None,
+                       device=None, min_blocks: int = 1) -> torch.Tensor:
+    """An uninitialised ``(blocks, n_images, rows_per_block)`` float32 table for
+    :func:`nearest_pool`, backed by ``musc_b200_nearest_pool_bytes`` (the table plus the
+    kernel's scheduler word).  ``min_blocks`` pads the block count (a reduce-scatter
+    over more ranks than blocks; the padding blocks are never filled)."""
+    rpb = rows if rows_per_block is None else rows_per_block
+    n_images = rows // patches
+    blocks = max(-(-rows // rpb), min_blocks)
+    nbytes = max(_lib.lib().musc_b200_nearest_pool_bytes(rows, patches, rpb), blocks * n_images * rpb * 4)
+    flat = torch.empty(-(-nbytes // 4), dtype=torch.float32, device=device)
+    return flat[:blocks * n_images * rpb].view(blocks, n_images, rpb)
+
+
 def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part: int = 0,
                  parts: int = 1, rows_per_block: int | None = None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
@@ -176,13 +190,16 @@ def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, par
 
     Evaluates part ``part`` of ``parts`` of the pool's symmetric tile list;
     with one part the single block is the full ``(n_images, rows)`` table.
+    ``out`` must come from :func:`nearest_pool_table` (it carries the scheduler word).
     """
     dev = bank.device
     rpb = rows if rows_per_block is None else rows_per_block
-    n_images = rows // patches
-    blocks = -(-rows // rpb)
     if out is None:
-        out = torch.empty(blocks, n_images, rpb, dtype=torch.float32, device=dev)
+        out = nearest_pool_table(rows, patches, rpb, dev)
+    need = _lib.lib().musc_b200_nearest_pool_bytes(rows, patches, rpb)
+    have = out.untyped_storage().nbytes() - out.storage_offset() * out.element_size()
+    if not out.is_contiguous() or have < need:
+        raise ValueError('nearest_pool: out must be a contiguous table from nearest_pool_table()')
     with torch.cuda.device(dev):
         st = _lib.lib().musc_b200_nearest_pool(_ptr(bank), rows, channels, patches, part, parts, rpb,
                                                _ptr(out), _stream(dev))

@@ -123,7 +123,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     rows = n_images * p
     q_rows = n_local * p
     rpb = per * p if world > 1 else rows
-    table = torch.empty(world if world > 1 else 1, n_images, rpb, dtype=torch.float32, device=dev)
+    table = kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world)
     mine = torch.empty(n_images, rpb, dtype=torch.float32, device=dev) if world > 1 else table[0]
     block_scores = torch.empty(rpb, dtype=torch.float64, device=dev)
     if world > 1:

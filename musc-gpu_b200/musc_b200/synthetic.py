@@ -54,6 +54,34 @@ def prototype_mixture(n_images: int, n_layers: int = 4, c: int = 1024, side: int
             for _ in range(n_layers)]
 
 
+def prototype_mixture_images(image_ids, n_layers: int = 4, c: int = 1024, side: int = 37,
+                             n_proto: int = 64, sigma: float = 0.1, anomaly_frac: float = 0.05,
+                             seed: int = 0, device='cpu') -> list[torch.Tensor]:
+    """The same mixture, drawn image by image: any subset of a pool (one rank's shard)
+    is generated without the rest.  Prototypes are seeded by (seed, layer) and each
+    image by (seed, layer, image id), so a pool is identical however it is sharded.
+    (Not the same stream as :func:`prototype_mixture`, which draws a pool sequentially.)
+    """
+    ids = list(image_ids)
+    p = side * side
+    dev = torch.device(device)
+    layers = []
+    for layer in range(n_layers):
+        g = torch.Generator(device=dev).manual_seed((seed * 1_000_003 + layer) * 7919 + 17)
+        protos = torch.randn(n_proto, c, generator=g, device=dev)
+        protos = protos / protos.norm(dim=1, keepdim=True)
+        tokens = torch.zeros(len(ids), p + 1, c, device=dev)
+        for k, img in enumerate(ids):
+            gi = torch.Generator(device=dev).manual_seed(((seed * 1_000_003 + layer) * 1_000_033 + img) * 31 + 5)
+            idx = torch.randint(0, n_proto, (p,), generator=gi, device=dev)
+            body = protos[idx] + sigma * torch.randn(p, c, generator=gi, device=dev)
+            mask = torch.rand(p, generator=gi, device=dev) < anomaly_frac
+            body[mask] = torch.randn(int(mask.sum()), c, generator=gi, device=dev)
+            tokens[k, 1:] = body
+        layers.append(tokens)
+    return layers
+
+
 def random_images(n_images: int, size: int = 518, seed: int = 0) -> torch.Tensor:
     """Images in [0, 1], shape ``(n_images, 3, size, size)`` fp32 (CPU)."""
     g = torch.Generator().manual_seed(seed)

@@ -43,6 +43,10 @@ class OracleKernels:
         out.copy_(torch.from_numpy(olnamd.l2_normalize(z) if l2_normalize else z))
 
     @staticmethod
+    def nearest_pool_table(rows, patches, rpb, device, min_blocks=1):
+        return torch.empty(max(-(-rows // rpb), min_blocks), rows // patches, rpb)
+
+    @staticmethod
     def prep_bank(z):
         return z.clone()
 
