@@ -61,6 +61,8 @@ def _args():
                     help='BASELINE.json config: 2 (default, the metric\'s), 3 super-fast, 4 N=1024, '
                          '5 encoder end to end')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--collective-sms', type=int, default=0,
+                    help='SMs left free for NCCL during each bank GEMM (multi-GPU; 0 = none)')
     return ap.parse_args()
 
 
@@ -250,6 +252,11 @@ def run_b200(args):
     group = None
     if world > 1:
         import datetime
+        if args.collective_sms > 0:
+            # The bank GEMM leaves `collective_sms` SMs free; NCCL's channels (one CTA
+            # each) must all fit there to run beside it.
+            os.environ.setdefault('NCCL_MAX_CTAS', str(args.collective_sms))
+            os.environ.setdefault('NCCL_MAX_NCHANNELS', str(args.collective_sms))
         dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=300))
         group = dist.group.WORLD
 
@@ -281,6 +288,8 @@ def run_b200(args):
     class Kernels:
         trimmed_ranks = staticmethod(ops.trimmed_ranks)
         nearest_pool_table = staticmethod(ops.nearest_pool_table)
+        empty_bank = staticmethod(ops.empty_bank)
+        bank_planes = staticmethod(ops.bank_planes)
     kern = Kernels()
 
     def counted(name):
@@ -301,10 +310,17 @@ def run_b200(args):
     for name in per_call:
         setattr(kern, name, counted(name))
     orig_attention = ops.attention
+    attn_events = []
 
     def counted_attention(*a, **k):
         launches[0] += 1
-        return orig_attention(*a, **k)
+        st = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        out = orig_attention(*a, **k)
+        e1.record(st)
+        attn_events.append((e0, e1, a[0].shape[0], a[0].shape[1], a[3]))
+        return out
     ops.attention = counted_attention
 
     def tokens_of(inputs):
@@ -320,7 +336,8 @@ def run_b200(args):
 
     def step(inputs, ready=None):
         return pipeline.score_pool(tokens_of(inputs), n_images=pool, radii=radii, group=group, kernels=kern,
-                                   super_fast_side=sf, ready=None if encoder is not None else ready)
+                                   super_fast_side=sf, ready=None if encoder is not None else ready,
+                                   collective_sms=args.collective_sms)
 
     def barrier():
         if group is not None:
@@ -330,6 +347,7 @@ def run_b200(args):
         step(resident)
     torch.cuda.synchronize()
     near_events.clear()
+    attn_events.clear()
     launches[0] = 0
     barrier()
     torch.cuda.synchronize()
@@ -344,6 +362,9 @@ def run_b200(args):
     barrier()
     elapsed_ms = t0.elapsed_time(t1)
     near_ms = [a.elapsed_time(b) for a, b in near_events]
+    # attention: 4 * L^2 * d flop per (batch item, head), head_dim 64
+    attn_ms = sum(e0.elapsed_time(e1) for e0, e1, *_ in attn_events)
+    attn_flop = sum(4.0 * length * length * 64 * bsz * heads for _, _, bsz, length, heads in attn_events)
     launches_timed = launches[0]
 
     # ---- e2e: pinned host inputs in (per-layer copies on a side stream, each layer's
@@ -424,6 +445,13 @@ def run_b200(args):
         }
         if args.config == '5':
             line['dtype'] = 'f32 scoring, fp16 encoder'
+            if attn_ms > 0:
+                at = attn_flop / (attn_ms / 1e3) / 1e12
+                line['attention'] = {'kernel': 'attention_kernel', 'bound': 'tensor', 'achieved': at,
+                                     'peak': peaks.get('bf16_tflops'), 'unit': 'TFLOP/s',
+                                     'frac': at / peaks.get('bf16_tflops'), 'launches': len(attn_events),
+                                     'ms_per_step': attn_ms / args.steps,
+                                     'peak_kind': f'{peak_kind} bf16 burst (short launches)'}
         if not args.no_cpu_baseline and args.config == '2':
             sys.path.insert(0, str(REPO))
             sample = CpuSample(pool)

@@ -126,6 +126,12 @@ int musc_b200_lnamd_super_fast(const void* tokens, int dtype, int n_images,
  * ---------------------------------------------------------------------- */
 size_t musc_b200_bank_bytes(long long rows, int channels);
 
+/* Byte offsets of the bank's four planes (hi, lo, |z|^2, 2^-k) for `rows` rows.
+ * The hi/lo planes hold rows * channels fp16 each and the vectors rows fp32,
+ * row-contiguous, so the banks of consecutive row blocks (one per rank) are
+ * gathered plane by plane into the bank of the concatenated rows. */
+int musc_b200_bank_layout(long long rows, int channels, size_t* plane_offsets);
+
 /* z: [rows][channels] fp32, channels % 8 == 0.  bank: >= bank_bytes. */
 int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
                         size_t bank_bytes, musc_b200_stream stream);
@@ -151,21 +157,26 @@ int musc_b200_nearest(const void* query_bank, long long query_rows, long long qu
  * the tensor-core work.  The tile list is split into n_parts balanced parts
  * and this call evaluates part `part` (multi-GPU: one part per rank, then an
  * element-wise MIN reduction of the tables).
+ * The bank is laid out for bank_rows >= rows rows (a padded, gathered bank);
+ * only its first `rows` rows are scored.
  * Layout: nearest_sq[block][image][r], block = row / rows_per_block,
  * r = row % rows_per_block, n_images = rows / patches_per_image; the call
  * first fills the whole table with FLT_MAX.  The buffer must hold
  * musc_b200_nearest_pool_bytes: the table plus a 256-byte word after it (at
  * the table size rounded up to 256 bytes) that the kernel's dynamic tile
  * scheduler uses; CTAs claim tiles from it, so ones that start late take
- * fewer.
+ * fewer.  max_ctas (0 = one per SM) caps the persistent grid: a multi-GPU
+ * caller leaves a few SMs free so the collectives of the neighbouring banks
+ * (which cannot share an SM with this kernel's 197 KB of shared memory) run
+ * concurrently instead of after it.
  * rows_per_block = rows gives the plain [image][row] table;
  * rows_per_block = one rank's rows makes each rank's rows contiguous for a
  * reduce-scatter. */
 size_t musc_b200_nearest_pool_bytes(long long rows, int patches_per_image, long long rows_per_block);
 
-int musc_b200_nearest_pool(const void* bank, long long rows, int channels, int patches_per_image,
-                           int part, int n_parts, long long rows_per_block, float* nearest_sq,
-                           musc_b200_stream stream);
+int musc_b200_nearest_pool(const void* bank, long long bank_rows, long long rows, int channels,
+                           int patches_per_image, int part, int n_parts, long long rows_per_block,
+                           int max_ctas, float* nearest_sq, musc_b200_stream stream);
 
 /* Interval average: scores[q] = mean of ranks [rank_lo, rank_hi) of
  * sqrt(nearest_sq[:, q]) over the n_images - 1 other images, in float32,

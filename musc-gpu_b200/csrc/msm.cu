@@ -771,9 +771,10 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   return check_launch("nearest_kernel<directed>");
 }
 
-int nearest_pool_launch(const void* bank, long long rows, int channels, int patches, int part, int parts,
-                        long long rows_per_block, float* nearest_sq, cudaStream_t s) {
-  const BankLayout l = bank_layout(rows, channels);
+int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
+                        int part, int parts, long long rows_per_block, int max_ctas, float* nearest_sq,
+                        cudaStream_t s) {
+  const BankLayout l = bank_layout(bank_rows, channels);
   const uint8_t* b = static_cast<const uint8_t*>(bank);
   CUtensorMap mah, mal, mbh, mbl;
   MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, nearest::BM));
@@ -807,7 +808,8 @@ int nearest_pool_launch(const void* bank, long long rows, int channels, int patc
   sym_part_range(rows, patches, n_images, p.num_m, p.num_n, part, parts, &p.tile_begin, &p.tile_end);
   if (p.tile_end <= p.tile_begin) return MUSC_B200_OK;  // nothing to do for this part
   MUSC_TRY(set_smem_attr());
-  const int grid = sm_count();
+  const int sms = sm_count();
+  const int grid = max_ctas > 0 && max_ctas < sms ? max_ctas : sms;
   nearest::nearest_kernel<true><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mah, mal, mbh, mbl, p);
   return check_launch("nearest_kernel<symmetric>");
 }
@@ -878,10 +880,22 @@ extern "C" size_t musc_b200_nearest_pool_bytes(long long rows, int patches_per_i
   return (table + 255) / 256 * 256 + 256;  // + the dynamic scheduler's counter
 }
 
-extern "C" int musc_b200_nearest_pool(const void* bank, long long rows, int channels, int patches_per_image,
-                                      int part, int n_parts, long long rows_per_block, float* nearest_sq,
-                                      musc_b200_stream stream) {
+extern "C" int musc_b200_bank_layout(long long rows, int channels, size_t* plane_offsets) {
   MUSC_TRY(check_bank_args(rows, channels));
+  if (!plane_offsets) return fail(MUSC_B200_ERR_INVALID, "bank_layout: null output");
+  const BankLayout l = bank_layout(rows, channels);
+  plane_offsets[0] = l.hi;
+  plane_offsets[1] = l.lo;
+  plane_offsets[2] = l.norm;
+  plane_offsets[3] = l.inv;
+  return MUSC_B200_OK;
+}
+
+extern "C" int musc_b200_nearest_pool(const void* bank, long long bank_rows, long long rows, int channels,
+                                      int patches_per_image, int part, int n_parts, long long rows_per_block,
+                                      int max_ctas, float* nearest_sq, musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(rows, channels));
+  if (bank_rows < rows) return fail(MUSC_B200_ERR_INVALID, "nearest_pool: bank_rows must be >= rows");
   if (!bank || !nearest_sq) return fail(MUSC_B200_ERR_INVALID, "nearest_pool: null pointer");
   if (reinterpret_cast<uintptr_t>(bank) % 1024 != 0)
     return fail(MUSC_B200_ERR_INVALID, "nearest_pool: bank must be 1024-byte aligned");
@@ -894,8 +908,8 @@ extern "C" int musc_b200_nearest_pool(const void* bank, long long rows, int chan
   if (reinterpret_cast<uintptr_t>(nearest_sq) % 4 != 0)
     return fail(MUSC_B200_ERR_INVALID, "nearest_pool: output must be 4-byte aligned");
   MUSC_TRY(require_sm100());
-  return nearest_pool_launch(bank, rows, channels, patches_per_image, part, n_parts, rows_per_block,
-                             nearest_sq, reinterpret_cast<cudaStream_t>(stream));
+  return nearest_pool_launch(bank, bank_rows, rows, channels, patches_per_image, part, n_parts, rows_per_block,
+                             max_ctas, nearest_sq, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
@@ -933,6 +947,6 @@ extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, i
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* table = reinterpret_cast<float*>(ws + bank_size);
   MUSC_TRY(musc_b200_prep_bank(z, rows, c, ws, bank_size, stream));
-  MUSC_TRY(musc_b200_nearest_pool(ws, rows, c, p, 0, 1, rows, table, stream));
+  MUSC_TRY(musc_b200_nearest_pool(ws, rows, rows, c, p, 0, 1, rows, 0, table, stream));
   return musc_b200_trimmed_mean(table, rows, n, rank_lo, rank_hi, scores, stream);
 }

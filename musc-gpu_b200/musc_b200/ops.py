@@ -138,7 +138,7 @@ def trimmed_ranks(n_images: int, topmin_min: float = 0, topmin_max: float = 0.3)
     return a, b
 
 
-def prep_bank(z: torch.Tensor) -> torch.Tensor:
+def prep_bank(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Split-fp16 tensor-core operand bank of ``z`` ``(rows, C)`` fp32."""
     _require_cuda(z, 'prep_bank')
     if z.ndim != 2 or z.dtype != torch.float32:
@@ -149,7 +149,7 @@ def prep_bank(z: torch.Tensor) -> torch.Tensor:
     with torch.cuda.device(dev):
         lib = _lib.lib()
         nbytes = lib.musc_b200_bank_bytes(rows, c)
-        bank = _aligned_empty(nbytes, dev)
+        bank = _aligned_empty(nbytes, dev) if out is None else out
         _lib.check(lib.musc_b200_prep_bank(_ptr(z), rows, c, _ptr(bank), nbytes, _stream(dev)),
                    'musc_b200_prep_bank')
     return bank
@@ -183,14 +183,32 @@ def nearest_pool_table(rows: int, patches: int, rows_per_block: int | None = Non
     return flat[:blocks * n_images * rpb].view(blocks, n_images, rpb)
 
 
+def empty_bank(rows: int, channels: int, device) -> torch.Tensor:
+    """An uninitialised, 1024-byte aligned bank buffer for ``rows`` rows."""
+    return _aligned_empty(_lib.lib().musc_b200_bank_bytes(rows, channels), torch.device(device))
+
+
+def bank_planes(bank: torch.Tensor, rows: int, channels: int, layout_rows: int | None = None):
+    """uint8 views of the first ``rows`` rows of each plane (hi, lo, |z|^2, 2^-k) of a bank
+    laid out for ``layout_rows`` rows -- the pieces a rank contributes to a gathered bank."""
+    layout_rows = rows if layout_rows is None else layout_rows
+    offs = (ctypes.c_size_t * 4)()
+    _lib.check(_lib.lib().musc_b200_bank_layout(layout_rows, channels, offs), 'musc_b200_bank_layout')
+    sizes = (rows * channels * 2, rows * channels * 2, rows * 4, rows * 4)
+    return [bank[o:o + n] for o, n in zip(offs, sizes)]
+
+
 def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part: int = 0,
                  parts: int = 1, rows_per_block: int | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, bank_rows: int | None = None,
+                 max_ctas: int = 0) -> torch.Tensor:
     """Symmetric pool minima: ``(blocks, n_images, rows_per_block)`` squared, FLT_MAX where unset.
 
     Evaluates part ``part`` of ``parts`` of the pool's symmetric tile list;
     with one part the single block is the full ``(n_images, rows)`` table.
     ``out`` must come from :func:`nearest_pool_table` (it carries the scheduler word).
+    ``bank_rows``: the row count the bank is laid out for (a padded gathered bank).
+    ``max_ctas``: cap on the persistent grid (0 = one CTA per SM).
     """
     dev = bank.device
     rpb = rows if rows_per_block is None else rows_per_block
@@ -201,8 +219,9 @@ def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, par
     if not out.is_contiguous() or have < need:
         raise ValueError('nearest_pool: out must be a contiguous table from nearest_pool_table()')
     with torch.cuda.device(dev):
-        st = _lib.lib().musc_b200_nearest_pool(_ptr(bank), rows, channels, patches, part, parts, rpb,
-                                               _ptr(out), _stream(dev))
+        st = _lib.lib().musc_b200_nearest_pool(_ptr(bank), rows if bank_rows is None else bank_rows, rows,
+                                               channels, patches, part, parts, rpb, int(max_ctas), _ptr(out),
+                                               _stream(dev))
         _lib.check(st, 'musc_b200_nearest_pool')
     return out
 

@@ -55,7 +55,8 @@ class PoolScores:
 def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
                radii: Sequence[int] = (1, 3, 5), topmin_min: float = 0, topmin_max: float = 0.3,
                image_size: int = 518, super_fast_side: int | None = None,
-               group=None, kernels=ops, ready: Sequence | None = None) -> PoolScores:
+               group=None, kernels=ops, ready: Sequence | None = None,
+               collective_sms: int = 16) -> PoolScores:
     """Score one pool from device-resident tokens.
 
     ``tokens``: per hooked layer, this rank's ``(n_local, 1+P, C)`` tokens
@@ -68,6 +69,8 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     host-to-device copy on another stream); the current stream waits on layer
     l's event just before that layer's LNAMD, so later layers' copies overlap
     the scoring of earlier ones.  Banks are processed layer by layer.
+    ``collective_sms``: with a process group, SMs left free during each bank's
+    GEMM so the neighbouring banks' gather and reduce-scatter run alongside it.
     """
     import torch.distributed as dist
 
@@ -114,46 +117,70 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         else:
             kernels.lnamd(t, radii, True, out=[local[li, ri, :n_local] for ri in range(n_r)])
 
-    # 2. Per bank: (gather), prep, symmetric nearest minima, interval average.
-    #    Rank r evaluates part r of the pool's symmetric tile list into a table
-    #    whose blocks are the ranks' query rows; a MIN reduce-scatter hands each
-    #    rank the minima of its own rows.
+    # 2. Per bank: prep, (gather), symmetric nearest minima, interval average.
+    #    One GPU: prep the whole bank, one symmetric launch, select.
+    #    G GPUs: each rank preps the bank of its own rows; the four bank planes are
+    #    all-gathered into a padded pool bank (the next bank's gather overlaps this
+    #    bank's GEMM); rank r evaluates part r of the symmetric tile list into a table
+    #    whose blocks are the ranks' query rows; a MIN reduce-scatter (overlapping the
+    #    next bank's GEMM) hands each rank the minima of its own rows.
     banks = [(li, ri) for li in range(n_l) for ri in range(n_r)]
     scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
     rows = n_images * p
     q_rows = n_local * p
     rpb = per * p if world > 1 else rows
-    table = kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world)
-    mine = torch.empty(n_images, rpb, dtype=torch.float32, device=dev) if world > 1 else table[0]
-    block_scores = torch.empty(rpb, dtype=torch.float64, device=dev)
-    if world > 1:
-        full = [torch.empty(world * per, p, c, dtype=torch.float32, device=dev) for _ in range(2)]
-        works = [None] * len(banks)
-        aggregate(banks[0][0])
-        works[0] = dist.all_gather_into_tensor(full[0], local[banks[0]], group=group, async_op=True)
-    for k, (li, ri) in enumerate(banks):
-        if world > 1:
-            if k + 1 < len(banks):
-                nxt = banks[k + 1]
-                aggregate(nxt[0])
-                works[k + 1] = dist.all_gather_into_tensor(full[(k + 1) % 2], local[nxt], group=group,
-                                                           async_op=True)
-            works[k].wait()
-            z_full = full[k % 2][:n_images]
-        else:
-            aggregate(li)
-            z_full = local[li, ri, :n_images]
-        bank = kernels.prep_bank(z_full.reshape(rows, c))
-        kernels.nearest_pool(bank, rows, c, p, rank, world, rpb, out=table)
-        if world > 1:
-            _min_reduce_scatter(table, mine, rank, group)
+
+    def select(near: torch.Tensor, li: int, ri: int) -> None:
         if q_rows == 0:
-            continue
+            return
         if q_rows == rpb:
-            kernels.trimmed_mean(mine, a, b, out=scores[ri, li].view(-1))
+            kernels.trimmed_mean(near, a, b, out=scores[ri, li].view(-1))
         else:
-            kernels.trimmed_mean(mine, a, b, out=block_scores)
-            scores[ri, li].view(-1).copy_(block_scores[:q_rows])
+            tmp = torch.empty(rpb, dtype=torch.float64, device=dev)
+            kernels.trimmed_mean(near, a, b, out=tmp)
+            scores[ri, li].view(-1).copy_(tmp[:q_rows])
+
+    if world == 1:
+        table = kernels.nearest_pool_table(rows, p, rows, dev)
+        bank = kernels.empty_bank(rows, c, dev)
+        for li, ri in banks:
+            aggregate(li)
+            kernels.prep_bank(local[li, ri, :n_images].reshape(rows, c), out=bank)
+            kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, out=table)
+            select(table[0], li, ri)
+    else:
+        local_rows, bank_rows = per * p, world * per * p
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
+        max_ctas = max(1, sms - collective_sms) if sms else 0
+        local_bank = [kernels.empty_bank(local_rows, c, dev) for _ in range(2)]
+        full_bank = [kernels.empty_bank(bank_rows, c, dev) for _ in range(2)]
+        tables = [kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world) for _ in range(2)]
+        mine = [torch.empty(n_images, rpb, dtype=torch.float32, device=dev) for _ in range(2)]
+
+        def start_gather(k):
+            li, ri = banks[k]
+            aggregate(li)
+            kernels.prep_bank(local[li, ri].reshape(local_rows, c), out=local_bank[k % 2])
+            pieces = zip(kernels.bank_planes(full_bank[k % 2], bank_rows, c),
+                         kernels.bank_planes(local_bank[k % 2], local_rows, c))
+            return [dist.all_gather_into_tensor(f, l, group=group, async_op=True) for f, l in pieces]
+
+        gathers = {0: start_gather(0)}
+        pending = None   # (finish_reduce_scatter, k) of the previous bank
+        for k, (li, ri) in enumerate(banks):
+            if k + 1 < len(banks):
+                gathers[k + 1] = start_gather(k + 1)
+            for w in gathers.pop(k):
+                w.wait()
+            kernels.nearest_pool(full_bank[k % 2], rows, c, p, rank, world, rpb, out=tables[k % 2],
+                                 bank_rows=bank_rows, max_ctas=max_ctas)
+            finish = _min_reduce_scatter(tables[k % 2], mine[k % 2], rank, group)
+            if pending is not None:
+                pending[0]()
+                select(mine[pending[1] % 2], *banks[pending[1]])
+            pending = (finish, k)
+        pending[0]()
+        select(mine[pending[1] % 2], *banks[pending[1]])
 
     # 3. Layer/radius means, up-sampling, image maxima for the local images.
     if n_local:
@@ -164,14 +191,21 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     return PoolScores(scores, maps, image_max, first, n_images)
 
 
-def _min_reduce_scatter(table: torch.Tensor, out: torch.Tensor, rank: int, group) -> None:
-    """Element-wise MIN over ranks of ``table`` (G, N, rpb); rank r keeps block r."""
+def _min_reduce_scatter(table: torch.Tensor, out: torch.Tensor, rank: int, group):
+    """Start an element-wise MIN over ranks of ``table`` (G, N, rpb) of which rank r keeps
+    block r in ``out``; returns a callable that completes it (the stream then waits)."""
     import torch.distributed as dist
     if dist.get_backend(group) == 'nccl':
-        dist.reduce_scatter_tensor(out, table, op=dist.ReduceOp.MIN, group=group)
-    else:  # gloo (CPU tests of the sharding logic) has no reduce-scatter
-        dist.all_reduce(table, op=dist.ReduceOp.MIN, group=group)
+        work = dist.reduce_scatter_tensor(out, table[:dist.get_world_size(group)], op=dist.ReduceOp.MIN,
+                                          group=group, async_op=True)
+        return work.wait
+    # gloo (CPU tests of the sharding logic) has no reduce-scatter
+    work = dist.all_reduce(table, op=dist.ReduceOp.MIN, group=group, async_op=True)
+
+    def finish():
+        work.wait()
         out.copy_(table[rank])
+    return finish
 
 
 def gather_pool(result: PoolScores, group=None) -> tuple[torch.Tensor, torch.Tensor]:

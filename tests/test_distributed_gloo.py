@@ -47,14 +47,25 @@ class OracleKernels:
         return torch.empty(max(-(-rows // rpb), min_blocks), rows // patches, rpb)
 
     @staticmethod
-    def prep_bank(z):
-        return z.clone()
+    def empty_bank(rows, c, device):
+        return torch.empty(rows, c)
 
     @staticmethod
-    def nearest_pool(bank, rows, c, p, part, parts, rpb, out):
+    def bank_planes(bank, rows, c, layout_rows=None):
+        return [bank[:rows].reshape(-1)]
+
+    @staticmethod
+    def prep_bank(z, out=None):
+        if out is None:
+            return z.clone()
+        out[:z.shape[0]].copy_(z)
+        return out
+
+    @staticmethod
+    def nearest_pool(bank, rows, c, p, part, parts, rpb, out, bank_rows=None, max_ctas=0):
         """Squared minima for the image pairs {i, j} with min(i, j) % parts == part."""
         n = rows // p
-        z = bank.numpy().reshape(n, p, c).astype(np.float64)
+        z = bank[:rows].numpy().reshape(n, p, c).astype(np.float64)
         out.fill_(float(np.finfo(np.float32).max))
         for i in range(n):
             for j in range(n):
