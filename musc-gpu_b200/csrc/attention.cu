@@ -11,10 +11,12 @@
 //   warp 1     one thread issues tcgen05.mma: S_j = Q K_j^T (128x128x64) into a
 //              double-buffered TMEM S, and PV_j = P_j V_j (128x64x128) into a
 //              double-buffered TMEM PV (V is the MN-major B operand);
-//   warps 2-5  softmax, one thread per query row: tcgen05.ld of S_j, online
-//              max / exp2 / row sum in fp32, P_j written to shared memory in
-//              the input type, K-major 128-byte swizzle layout the MMA reads; one
-//              tile later the same thread reads PV_j and accumulates
+//   warps 2-9  softmax, two warps per query row (one per 64-key half of the
+//              tile, exchanging partial row maxima through shared memory):
+//              tcgen05.ld of S_j, online max / exp2 / row sum in fp32, P_j
+//              written to shared memory in the input type, K-major 128-byte
+//              swizzle layout the MMA reads; one tile later the same threads
+//              read their 32 output dims of PV_j and accumulate
 //              O = O * alpha_j + PV_j in registers (so the tensor core never
 //              waits for a rescale); finally O / l goes out in the input type.
 // QK_{j+1} overlaps softmax_j; PV_j overlaps softmax_{j+1}.
@@ -35,7 +37,7 @@ constexpr int D = 64;         // head dim: one 128-byte swizzle row of bf16
 constexpr int KV_STAGES = 2;
 constexpr int TILE_BYTES = BKV * D * 2;  // 16 KB (Q, K_j, V_j tiles)
 constexpr int P_BYTES = BQ * BKV * 2;    // 32 KB (two 64-key swizzle column blocks)
-constexpr int SOFTMAX_WARPS = 4;
+constexpr int SOFTMAX_WARPS = 8;  // two per TMEM lane quarter
 constexpr int THREADS = 32 * (2 + SOFTMAX_WARPS);
 constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0;      // S buffers at columns 0 and 128
@@ -59,6 +61,7 @@ struct Smem {
   uint64_t p_full[2];
   uint64_t o_full[2], o_empty[2];
   uint64_t drain;
+  float red[2][2][BQ];  // [tile parity][column half][row]: partial row maxima / final sums
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -95,6 +98,21 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
 __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr) {
   return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)(TILE_BYTES >> 4) << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Barrier of the two softmax warps that share a TMEM lane quarter (named barrier
+// 2 + quarter, 64 threads) that also ORs `flag` across them.
+__device__ __forceinline__ bool pair_sync_any(int quarter, bool flag) {
+  uint32_t res;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, 64, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(res)
+      : "r"((uint32_t)flag), "r"(2 + quarter)
+      : "memory");
+  return res != 0;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -259,27 +277,32 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
     }
   } else {
     // ------------------------------------------------------------ softmax + output
+    // Two warps per TMEM lane quarter: warp half h owns key columns [64h, 64h + 64) of S
+    // and output dims [32h, 32h + 32); the pair exchanges its partial row maxima once per
+    // tile through shared memory (named barrier 2 + quarter, 64 threads).  Every stop
+    // decision is taken at a pair barrier, so the two warps always leave together.
     const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
     const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* prow_base = nullptr;
-    float o[D];
+    float o[D / 2];
 #pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.f;
-    float m_run = -FLT_MAX, l_run = 0.f, alpha_prev = 1.f;
+    for (int d = 0; d < D / 2; ++d) o[d] = 0.f;
+    float m_run = -FLT_MAX, l_half = 0.f, alpha_prev = 1.f;
     bool ok = true;
-    for (int j = 0; j <= n_kv; ++j) {
-      if (j < n_kv) {
-        const int sb = j & 1;
-        const uint32_t sph = (uint32_t)(j >> 1) & 1u;
-        ok = wait_bounded(tc::smem_u32(&sm.s_full[sb]), sph, abort_flag, p.err);
-        if (__any_sync(0xffffffffu, !ok)) break;
+    int j = 0;
+    for (; j < n_kv; ++j) {
+      const int sb = j & 1;
+      ok = ok && wait_bounded(tc::smem_u32(&sm.s_full[sb]), (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      float sv[BKV / 2];
+      float mt = -FLT_MAX;
+      const int valid = p.tokens - j * BKV - half * (BKV / 2);  // keys past the sequence end are masked
+      if (__all_sync(0xffffffffu, ok)) {
         tc::fence_after_sync();
-        float sv[BKV];
 #pragma unroll
-        for (int c = 0; c < BKV / 32; ++c) {
+        for (int c = 0; c < BKV / 64; ++c) {
           uint32_t raw[32];
-          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(S_COL + sb * BKV + c * 32), raw);
+          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(S_COL + sb * BKV + half * (BKV / 2) + c * 32), raw);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(raw[t]);
@@ -287,84 +310,92 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.s_empty[sb]));
-        const int valid = p.tokens - j * BKV;  // keys past the sequence end are masked
-        float mt = -FLT_MAX;
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) {
+        for (int c = 0; c < BKV / 2; ++c) {
           sv[c] = c < valid ? sv[c] * p.scale_log2 : -FLT_MAX;
           mt = fmaxf(mt, sv[c]);
         }
-        const float m_new = fmaxf(m_run, mt);
-        const float alpha = ex2(m_run - m_new);
-        float lsum = 0.f;
-        prow_base = sm.p[sb] + r * 128;
+        sm.red[j & 1][half][r] = mt;
+      } else {
+        ok = false;
+      }
+      if (pair_sync_any(quarter, !ok)) break;
+      mt = fmaxf(mt, sm.red[j & 1][half ^ 1][r]);
+      const float m_new = fmaxf(m_run, mt);
+      const float alpha = ex2(m_run - m_new);
+      float lsum = 0.f;
+      uint8_t* prow = sm.p[sb] + half * (BQ * 128) + r * 128;  // this half's 64-key column block
 #pragma unroll
-        for (int ch = 0; ch < BKV / 8; ++ch) {  // 16-byte chunks of 8 keys
-          float e[8];
+      for (int ch = 0; ch < BKV / 16; ++ch) {  // 16-byte chunks of 8 keys
+        float e[8];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const int c = ch * 8 + t;
-            e[t] = c < valid ? ex2(sv[c] - m_new) : 0.f;
-            lsum += e[t];
-          }
-          uint4 pk = make_uint4(pack2<FP16>(e[0], e[1]), pack2<FP16>(e[2], e[3]), pack2<FP16>(e[4], e[5]),
-                                pack2<FP16>(e[6], e[7]));
-          const int blk = ch >> 3, cc = ch & 7;  // 64-key column block, chunk within the 128-byte row
-          *reinterpret_cast<uint4*>(prow_base + blk * (BQ * 128) + ((cc ^ (r & 7)) << 4)) = pk;
+        for (int t = 0; t < 8; ++t) {
+          const int c = ch * 8 + t;
+          e[t] = c < valid ? ex2(sv[c] - m_new) : 0.f;
+          lsum += e[t];
         }
-        l_run = l_run * alpha + lsum;
-        m_run = m_new;
-        tc::fence_proxy_async_smem();  // P stores -> visible to the tensor core
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.p_full[sb]));
-        if (j >= 1) {
-          // accumulate PV_{j-1}
-          const int pb = (j - 1) & 1;
-          const uint32_t pph = (uint32_t)((j - 1) >> 1) & 1u;
-          ok = wait_bounded(tc::smem_u32(&sm.o_full[pb]), pph, abort_flag, p.err);
-          if (__any_sync(0xffffffffu, !ok)) break;
+        uint4 pk = make_uint4(pack2<FP16>(e[0], e[1]), pack2<FP16>(e[2], e[3]), pack2<FP16>(e[4], e[5]),
+                              pack2<FP16>(e[6], e[7]));
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
+      }
+      l_half = l_half * alpha + lsum;
+      m_run = m_new;
+      tc::fence_proxy_async_smem();  // P stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.p_full[sb]));
+      if (j >= 1) {
+        // accumulate this half's dims of PV_{j-1}
+        const int pb = (j - 1) & 1;
+        ok = wait_bounded(tc::smem_u32(&sm.o_full[pb]), (uint32_t)((j - 1) >> 1) & 1u, abort_flag, p.err);
+        if (__all_sync(0xffffffffu, ok)) {
           tc::fence_after_sync();
+          uint32_t raw[32];
+          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(PV_COL + pb * D + half * 32), raw);
+          tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t raw[32];
-            tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(PV_COL + pb * D + c * 32), raw);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int t = 0; t < 32; ++t) o[c * 32 + t] = fmaf(o[c * 32 + t], alpha_prev, __uint_as_float(raw[t]));
-          }
+          for (int t = 0; t < 32; ++t) o[t] = fmaf(o[t], alpha_prev, __uint_as_float(raw[t]));
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.o_empty[pb]));
-        }
-        alpha_prev = alpha;
-      } else {
-        // last PV
-        const int pb = (n_kv - 1) & 1;
-        const uint32_t pph = (uint32_t)((n_kv - 1) >> 1) & 1u;
-        ok = wait_bounded(tc::smem_u32(&sm.o_full[pb]), pph, abort_flag, p.err);
-        if (__any_sync(0xffffffffu, !ok)) break;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t raw[32];
-          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(PV_COL + pb * D + c * 32), raw);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int t = 0; t < 32; ++t) o[c * 32 + t] = fmaf(o[c * 32 + t], alpha_prev, __uint_as_float(raw[t]));
+        } else {
+          ok = false;
         }
       }
+      alpha_prev = alpha;
     }
-    const int token = q_tile * BQ + r;
-    if (ok && token < p.tokens) {
-      const float inv = 1.f / l_run;
-      uint16_t* dst = static_cast<uint16_t*>(p.out) + ((long long)b * p.tokens + token) * p.out_row_stride + h * D;
+    if (j == n_kv) {
+      // last PV
+      const int pb = (n_kv - 1) & 1;
+      ok = ok && wait_bounded(tc::smem_u32(&sm.o_full[pb]), (uint32_t)((n_kv - 1) >> 1) & 1u, abort_flag, p.err);
+      if (__all_sync(0xffffffffu, ok)) {
+        tc::fence_after_sync();
+        uint32_t raw[32];
+        tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(PV_COL + pb * D + half * 32), raw);
+        tc::tmem_wait_ld();
 #pragma unroll
-      for (int c8 = 0; c8 < D / 8; ++c8) {
-        uint4 pk = make_uint4(pack2<FP16>(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv),
-                              pack2<FP16>(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
-                              pack2<FP16>(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
-                              pack2<FP16>(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
-        *reinterpret_cast<uint4*>(dst + c8 * 8) = pk;
+        for (int t = 0; t < 32; ++t) o[t] = fmaf(o[t], alpha_prev, __uint_as_float(raw[t]));
+      } else {
+        ok = false;
+      }
+      // row sum = both halves' partial sums, exchanged in the parity buffer the last
+      // tile did not use (the partner may still be reading the last tile's maxima)
+      const int pf = n_kv & 1;
+      sm.red[pf][half][r] = l_half;
+      const bool stop = pair_sync_any(quarter, !ok);
+      const float l_run = l_half + sm.red[pf][half ^ 1][r];
+      const int token = q_tile * BQ + r;
+      if (!stop && token < p.tokens) {
+        const float inv = 1.f / l_run;
+        uint16_t* dst = static_cast<uint16_t*>(p.out) + ((long long)b * p.tokens + token) * p.out_row_stride +
+                        h * D + half * 32;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 pk = make_uint4(pack2<FP16>(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv),
+                                pack2<FP16>(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv),
+                                pack2<FP16>(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv),
+                                pack2<FP16>(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv));
+          *reinterpret_cast<uint4*>(dst + c8 * 8) = pk;
+        }
       }
     }
   }
