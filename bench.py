@@ -292,19 +292,19 @@ def run_b200(args):
         bank_planes = staticmethod(ops.bank_planes)
     kern = Kernels()
 
+    op_events = {}
+
     def counted(name):
         fn = getattr(ops, name)
 
         def call(*a, **k):
             launches[0] += per_call[name]
-            if name != 'nearest_pool':
-                return fn(*a, **k)
             st = torch.cuda.current_stream(dev)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             out = fn(*a, **k)
             e1.record(st)
-            near_events.append((e0, e1))
+            (near_events if name == 'nearest_pool' else op_events.setdefault(name, [])).append((e0, e1))
             return out
         return call
     for name in per_call:
@@ -348,6 +348,7 @@ def run_b200(args):
     torch.cuda.synchronize()
     near_events.clear()
     attn_events.clear()
+    op_events.clear()
     launches[0] = 0
     barrier()
     torch.cuda.synchronize()
@@ -362,6 +363,8 @@ def run_b200(args):
     barrier()
     elapsed_ms = t0.elapsed_time(t1)
     near_ms = [a.elapsed_time(b) for a, b in near_events]
+    op_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / args.steps for name, evs in op_events.items()}
+    op_ms['nearest_pool'] = sum(near_ms) / args.steps
     # attention: 4 * L^2 * d flop per (batch item, head), head_dim 64
     attn_ms = sum(e0.elapsed_time(e1) for e0, e1, *_ in attn_events)
     attn_flop = sum(4.0 * length * length * 64 * bsz * heads for _, _, bsz, length, heads in attn_events)
@@ -442,6 +445,7 @@ def run_b200(args):
                          'launch_ms': near_avg_ms},
             'gpu_launches': launches_timed,
             'clocks': clocks.summary(),
+            'op_ms_per_step': {k: round(v, 3) for k, v in sorted(op_ms.items(), key=lambda kv: -kv[1])},
         }
         if args.config == '5':
             line['dtype'] = 'f32 scoring, fp16 encoder'

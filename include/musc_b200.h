@@ -56,6 +56,14 @@ const char* musc_b200_last_error(void);
  * (MUSC_B200_OK or MUSC_B200_ERR_TIMEOUT).  Synchronises the device. */
 int musc_b200_take_device_error(int* code);
 
+/* Self-test of the device-side bounded wait that every pipelined kernel here
+ * uses (no counterpart in the reference, whose kernels have no waits): a
+ * single thread waits on an mbarrier for at most limit_ns nanoseconds.  With
+ * arrive == 0 nothing arrives, the wait expires and the device error word
+ * becomes MUSC_B200_ERR_TIMEOUT (read it with musc_b200_take_device_error);
+ * with arrive != 0 it completes at once.  The context stays usable either way. */
+int musc_b200_selftest_wait(long long limit_ns, int arrive, musc_b200_stream stream);
+
 /* ------------------------------------------------------------------------
  * LNAMD
  * Replaces LNAMD._embed (models/modules/_LNAMD.py:72-129), its direct-pool

@@ -89,9 +89,6 @@ __device__ __forceinline__ float4 f4scale(float4 a, float s) {
   return make_float4(a.x * s, a.y * s, a.z * s, a.w * s);
 }
 __device__ __forceinline__ float f4dot(float4 a) { return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w; }
-__device__ __forceinline__ float4 f4div(float4 a, float d) {
-  return make_float4(a.x / d, a.y / d, a.z / d, a.w / d);
-}
 
 // Block-wide sum of up to three values; `buf` alternates between calls so a
 // single __syncthreads per call suffices.  Every thread gets the totals.
@@ -140,24 +137,29 @@ lnamd_stencil_kernel(const T* __restrict__ tokens, int tokens_per_image, int cha
   float* o3p = want3 ? out3 + (long long)img * out_image_stride + cg * 4 : nullptr;
   float* o5p = want5 ? out5 + (long long)img * out_image_stride + cg * 4 : nullptr;
 
-  for (int xp = 0; xp < side + 2; ++xp) {
-    float4 v1 = zero, v3 = zero, v5 = zero;
-    if (xp < side && active) {
-      float4 r[5];
+  // Software pipeline: the five rows of column x'+1 are loaded while column x' is
+  // reduced, so the loads overlap the per-patch block reduction.
+  float4 cur[5], nxt[5];
+  auto load_col = [&](int xc, float4 (&r)[5]) {
 #pragma unroll
-      for (int d = 0; d < 5; ++d) {
-        const int yy = y + d - 2;
-        if (yy >= 0 && yy < side) {
-          float4 t = load4<T>(body + ((long long)yy * side + xp) * channels);
-          r[d] = make_float4(t.x - mu, t.y - mu, t.z - mu, t.w - mu);
-        } else {
-          r[d] = zero;
-        }
+    for (int d = 0; d < 5; ++d) {
+      const int yy = y + d - 2;
+      if (xc < side && active && yy >= 0 && yy < side) {
+        float4 t = load4<T>(body + ((long long)yy * side + xc) * channels);
+        r[d] = make_float4(t.x - mu, t.y - mu, t.z - mu, t.w - mu);
+      } else {
+        r[d] = zero;
       }
-      v1 = r[2];
-      v3 = f4add(f4add(r[1], r[2]), r[3]);
-      v5 = f4add(f4add(v3, r[0]), r[4]);
     }
+  };
+  load_col(0, cur);
+  for (int xp = 0; xp < side + 2; ++xp) {
+    load_col(xp + 1, nxt);
+    const float4 v1 = cur[2];
+    const float4 v3 = f4add(f4add(cur[1], cur[2]), cur[3]);
+    const float4 v5 = f4add(f4add(v3, cur[0]), cur[4]);
+#pragma unroll
+    for (int d = 0; d < 5; ++d) cur[d] = nxt[d];
     a1[0] = a1[1]; a1[1] = a1[2]; a1[2] = v1;
     a3[0] = a3[1]; a3[1] = a3[2]; a3[2] = a3[3]; a3[3] = v3;
     a5[0] = a5[1]; a5[1] = a5[2]; a5[2] = a5[3]; a5[3] = a5[4]; a5[4] = v5;
@@ -170,9 +172,9 @@ lnamd_stencil_kernel(const T* __restrict__ tokens, int tokens_per_image, int cha
       float sq[3] = {want1 ? f4dot(o1) : 0.f, want3 ? f4dot(o3) : 0.f, want5 ? f4dot(o5) : 0.f};
       if (!active) sq[0] = sq[1] = sq[2] = 0.f;
       block_sum<3>(sq, red, x & 1);
-      o1 = f4div(o1, sqrtf(sq[0]));
-      o3 = f4div(o3, sqrtf(sq[1]));
-      o5 = f4div(o5, sqrtf(sq[2]));
+      o1 = f4scale(o1, 1.f / sqrtf(sq[0]));
+      o3 = f4scale(o3, 1.f / sqrtf(sq[1]));
+      o5 = f4scale(o5, 1.f / sqrtf(sq[2]));
     }
     if (active) {
       const long long off = (long long)(y * side + x) * out_patch_stride;
@@ -255,7 +257,7 @@ lnamd_super_fast_kernel(const T* __restrict__ tokens, int tokens_per_image, int 
       if (normalize) {
         float sq[1] = {active ? f4dot(o) : 0.f};
         block_sum<1>(sq, red, j & 1);
-        o = f4div(o, sqrtf(sq[0]));
+        o = f4scale(o, 1.f / sqrtf(sq[0]));
       }
       if (active) *reinterpret_cast<float4*>(op + (long long)(i * out_side + j) * out_patch_stride) = o;
       ++j;

@@ -98,3 +98,47 @@ extern "C" int musc_b200_take_device_error(int* code) {
   *code = value;
   return MUSC_B200_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded-wait path every pipelined kernel uses: one thread
+// initialises an mbarrier and waits on it with a time limit.  With `arrive`
+// == 0 nothing ever arrives, the wait expires after limit_ns, the kernel
+// records MUSC_B200_ERR_TIMEOUT in the device error word and returns -- the
+// context stays usable.  With `arrive` != 0 the thread arrives first and the
+// wait completes at once.
+// ---------------------------------------------------------------------------
+namespace musc {
+__global__ void selftest_wait_kernel(long long limit_ns, int arrive, int* err) {
+  __shared__ uint64_t bar;
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(a) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (arrive) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+  const uint64_t start = global_ns();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a)
+        : "memory");
+    if (done) return;
+    if ((long long)(global_ns() - start) > limit_ns) {
+      atomicExch(err, MUSC_B200_ERR_TIMEOUT);
+      return;
+    }
+  }
+}
+}  // namespace musc
+
+extern "C" int musc_b200_selftest_wait(long long limit_ns, int arrive, musc_b200_stream stream) {
+  if (limit_ns <= 0 || limit_ns > 10000000000LL)
+    return musc::fail(MUSC_B200_ERR_INVALID, "selftest_wait: limit_ns must be in (0, 1e10]");
+  MUSC_TRY(musc::require_sm100());
+  int* err = musc::device_error_ptr();
+  if (!err) return musc::fail(MUSC_B200_ERR_CUDA, "selftest_wait: device error word unavailable");
+  musc::selftest_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns, arrive, err);
+  return musc::check_launch("selftest_wait_kernel");
+}

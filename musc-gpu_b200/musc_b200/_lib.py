@@ -25,6 +25,7 @@ SIGNATURES = {
     'musc_b200_abi_version': (_int, []),
     'musc_b200_last_error': (ctypes.c_char_p, []),
     'musc_b200_take_device_error': (_int, [ctypes.POINTER(_int)]),
+    'musc_b200_selftest_wait': (_int, [_ll, _int, _vp]),
     'musc_b200_lnamd_workspace_bytes': (_sz, [_int]),
     'musc_b200_lnamd': (_int, [_vp, _int, _int, _int, _int, _int, ctypes.POINTER(_int),
                                ctypes.POINTER(_vp), _ll, _ll, _int, _vp, _sz, _vp]),
