@@ -151,11 +151,14 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     else:
         local_rows, bank_rows = per * p, world * per * p
         sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
-        max_ctas = max(1, sms - collective_sms) if sms else 0
+        max_ctas = max(1, sms - collective_sms) if (sms and collective_sms) else 0
+        # The gathers run on their own communicator (own NCCL stream), so bank k+1's gather
+        # is never queued behind bank k-1's reduce-scatter, which must wait for GEMM k-1.
+        gather_group = _side_group(group)
         local_bank = [kernels.empty_bank(local_rows, c, dev) for _ in range(2)]
         full_bank = [kernels.empty_bank(bank_rows, c, dev) for _ in range(2)]
-        tables = [kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world) for _ in range(2)]
-        mine = [torch.empty(n_images, rpb, dtype=torch.float32, device=dev) for _ in range(2)]
+        tables = [kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world) for _ in range(3)]
+        mine = [torch.empty(n_images, rpb, dtype=torch.float32, device=dev) for _ in range(3)]
 
         def start_gather(k):
             li, ri = banks[k]
@@ -163,24 +166,25 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
             kernels.prep_bank(local[li, ri].reshape(local_rows, c), out=local_bank[k % 2])
             pieces = zip(kernels.bank_planes(full_bank[k % 2], bank_rows, c),
                          kernels.bank_planes(local_bank[k % 2], local_rows, c))
-            return [dist.all_gather_into_tensor(f, l, group=group, async_op=True) for f, l in pieces]
+            return [dist.all_gather_into_tensor(f, l, group=gather_group, async_op=True) for f, l in pieces]
 
         gathers = {0: start_gather(0)}
-        pending = None   # (finish_reduce_scatter, k) of the previous bank
+        pending = []   # (finish_reduce_scatter, k), completed two banks later
         for k, (li, ri) in enumerate(banks):
             if k + 1 < len(banks):
                 gathers[k + 1] = start_gather(k + 1)
             for w in gathers.pop(k):
                 w.wait()
-            kernels.nearest_pool(full_bank[k % 2], rows, c, p, rank, world, rpb, out=tables[k % 2],
+            kernels.nearest_pool(full_bank[k % 2], rows, c, p, rank, world, rpb, out=tables[k % 3],
                                  bank_rows=bank_rows, max_ctas=max_ctas)
-            finish = _min_reduce_scatter(tables[k % 2], mine[k % 2], rank, group)
-            if pending is not None:
-                pending[0]()
-                select(mine[pending[1] % 2], *banks[pending[1]])
-            pending = (finish, k)
-        pending[0]()
-        select(mine[pending[1] % 2], *banks[pending[1]])
+            pending.append((_min_reduce_scatter(tables[k % 3], mine[k % 3], rank, group), k))
+            if len(pending) > 2:
+                finish, kk = pending.pop(0)
+                finish()
+                select(mine[kk % 3], *banks[kk])
+        for finish, kk in pending:
+            finish()
+            select(mine[kk % 3], *banks[kk])
 
     # 3. Layer/radius means, up-sampling, image maxima for the local images.
     if n_local:
@@ -189,6 +193,19 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         maps = torch.empty(0, side, side, dtype=torch.float64, device=dev)
         image_max = torch.empty(0, dtype=torch.float64, device=dev)
     return PoolScores(scores, maps, image_max, first, n_images)
+
+
+_SIDE_GROUPS: dict = {}
+
+
+def _side_group(group):
+    """A second communicator over the same ranks (created once per group, collectively)."""
+    import torch.distributed as dist
+    key = id(group)
+    if key not in _SIDE_GROUPS:
+        ranks = dist.get_process_group_ranks(group)
+        _SIDE_GROUPS[key] = dist.new_group(ranks=ranks, backend=dist.get_backend(group))
+    return _SIDE_GROUPS[key]
 
 
 def _min_reduce_scatter(table: torch.Tensor, out: torch.Tensor, rank: int, group):
