@@ -17,10 +17,10 @@
 //      d^2 = |q|^2 + |r|^2 - 2 q.r, keep a running minimum per reference
 //      image segment and atomically lower nearest_sq[image][row].  The
 //      N*P x N*P distance matrix never reaches memory.
-//   3. trimmed_mean_kernel: per query row, the sum of the smallest m
-//      distances by a binary search on the order-preserving bit pattern of
-//      the squared minima (exact threshold, ties handled by count), for
-//      m = rank_hi and rank_lo; score = mean of ranks [rank_lo, rank_hi)
+//   3. trimmed_mean_kernel: per query row (four threads), the sum of the
+//      smallest m distances by a binary search on the order-preserving bit
+//      pattern of the squared minima (exact threshold, ties handled by count),
+//      for m = rank_hi and rank_lo; score = mean of ranks [rank_lo, rank_hi)
 //      rounded to fp32 like the reference's fp32 mean, stored as float64.
 #include "common.cuh"
 #include "tc.cuh"
@@ -547,67 +547,99 @@ __global__ void fill_u32_kernel(unsigned int* p, long long n, unsigned int v) {
 }
 
 // ------------------------------------------------------------------ trimmed mean
-__device__ __forceinline__ int count_below(const unsigned int* col, int n, int stride, unsigned int t) {
-  int c = 0;
-  for (int j = 0; j < n; ++j) c += col[j * stride] < t ? 1 : 0;
-  return c;
+// Four threads (a quad) per query row: each pass of the threshold search counts a
+// quarter of the row's keys per thread and combines the counts with two shuffles,
+// so the sequential search passes are four times shorter.  The CTA stages a
+// [32 rows][pitch] transposed tile of the image-major table in shared memory
+// (pitch = 4 mod 32 words, so a warp's 8 rows x 4 quad lanes hit 32 banks).
+constexpr int kSelRows = 32;
+constexpr int kSelThreads = 4 * kSelRows;
+
+__device__ __forceinline__ int quad_sum(int v, unsigned mask) {
+  v += __shfl_xor_sync(mask, v, 1);
+  v += __shfl_xor_sync(mask, v, 2);
+  return v;
 }
 
-__device__ __forceinline__ double sum_below(const unsigned int* col, int n, int stride, unsigned int t) {
-  double s = 0.0;
-  for (int j = 0; j < n; ++j) {
-    const unsigned int k = col[j * stride];
-    if (k < t) s += (double)sqrtf(__uint_as_float(k));
+__device__ __forceinline__ double quad_sum(double v, unsigned mask) {
+  v += __shfl_xor_sync(mask, v, 1);
+  v += __shfl_xor_sync(mask, v, 2);
+  return v;
+}
+
+struct SelRow {
+  const unsigned int* keys;  // this row's keys in shared memory
+  int n, sub;
+  unsigned mask;
+
+  __device__ __forceinline__ int count_below(unsigned int t) const {
+    int c = 0;
+    for (int j = sub; j < n; j += 4) c += keys[j] < t ? 1 : 0;
+    return quad_sum(c, mask);
   }
-  return s;
-}
-
-// Sum of the m smallest sqrt(values) in the column (keys are non-negative
-// float bit patterns, so integer order is value order).
-__device__ double sum_smallest(const unsigned int* col, int n, int stride, int m, unsigned int kmin,
-                               unsigned int kmax) {
-  if (m <= 0) return 0.0;
-  const int k = m - 1;
-  unsigned int lo = kmin;            // count(< lo) == 0 <= k
-  unsigned int hi = kmax + 1u;       // count(< hi) == n > k
-  while (hi - lo > 1u) {
-    const unsigned int mid = lo + (hi - lo) / 2u;
-    const int c = count_below(col, n, stride, mid);
-    if (c <= k) {
-      lo = mid;
-    } else {
-      hi = mid;
-      if (c == m) return sum_below(col, n, stride, hi);
+  __device__ __forceinline__ double sum_below(unsigned int t) const {
+    double acc = 0.0;
+    for (int j = sub; j < n; j += 4) {
+      const unsigned int k = keys[j];
+      if (k < t) acc += (double)sqrtf(__uint_as_float(k));
     }
+    return quad_sum(acc, mask);
   }
-  // lo is the k-th smallest key: count(< lo) <= k < count(<= lo).
-  const int c_lo = count_below(col, n, stride, lo);
-  return sum_below(col, n, stride, lo) + (double)(m - c_lo) * (double)sqrtf(__uint_as_float(lo));
-}
+  // Sum of the m smallest sqrt(values) (keys are non-negative float bit patterns,
+  // so integer order is value order); a binary search for the m-th key, stopping
+  // as soon as exactly m keys lie below the bracket's upper end.
+  __device__ double sum_smallest(int m, unsigned int kmin, unsigned int kmax) const {
+    if (m <= 0) return 0.0;
+    const int k = m - 1;
+    unsigned int lo = kmin;        // count(< lo) == 0 <= k
+    unsigned int hi = kmax + 1u;   // count(< hi) == n > k
+    while (hi - lo > 1u) {
+      const unsigned int mid = lo + (hi - lo) / 2u;
+      const int c = count_below(mid);
+      if (c <= k) {
+        lo = mid;
+      } else {
+        hi = mid;
+        if (c == m) return sum_below(hi);
+      }
+    }
+    // lo is the k-th smallest key: count(< lo) <= k < count(<= lo).
+    const int c_lo = count_below(lo);
+    return sum_below(lo) + (double)(m - c_lo) * (double)sqrtf(__uint_as_float(lo));
+  }
+};
 
-__global__ void trimmed_mean_kernel(const unsigned int* __restrict__ nearest, long long q_rows, int n,
-                                    int rank_lo, int rank_hi, double* __restrict__ scores) {
-  extern __shared__ unsigned int keys[];  // [n][R], R = blockDim.x
-  const int R = blockDim.x;
-  const long long row0 = (long long)blockIdx.x * R;
-  for (int idx = threadIdx.x; idx < n * R; idx += R) {
-    const int j = idx / R, r = idx - j * R;
+__global__ void __launch_bounds__(kSelThreads)
+trimmed_mean_kernel(const unsigned int* __restrict__ nearest, long long q_rows, int n, int pitch,
+                    int rank_lo, int rank_hi, double* __restrict__ scores) {
+  extern __shared__ unsigned int tile[];  // [kSelRows][pitch]
+  const long long row0 = (long long)blockIdx.x * kSelRows;
+  for (int idx = threadIdx.x; idx < n * kSelRows; idx += kSelThreads) {
+    const int j = idx / kSelRows, r = idx - j * kSelRows;
     const long long row = row0 + r;
-    keys[idx] = row < q_rows ? __ldg(nearest + (long long)j * q_rows + row) : 0u;
+    tile[r * pitch + j] = row < q_rows ? __ldg(nearest + (long long)j * q_rows + row) : 0u;
   }
   __syncthreads();
-  const long long row = row0 + threadIdx.x;
-  if (row >= q_rows) return;
-  const unsigned int* col = keys + threadIdx.x;
+  const int r = threadIdx.x >> 2, sub = threadIdx.x & 3;
+  const long long row = row0 + r;
+  if (row >= q_rows) return;  // quad-uniform
+  const unsigned lane = threadIdx.x & 31;
+  SelRow sel{tile + r * pitch, n, sub, 0xFu << (lane & ~3u)};
   unsigned int kmin = 0xFFFFFFFFu, kmax = 0u;
-  for (int j = 0; j < n; ++j) {
-    const unsigned int k = col[j * R];
+  for (int j = sub; j < n; j += 4) {
+    const unsigned int k = sel.keys[j];
     kmin = k < kmin ? k : kmin;
     kmax = k > kmax ? k : kmax;
   }
-  const double hi = sum_smallest(col, n, R, rank_hi, kmin, kmax);
-  const double lo = sum_smallest(col, n, R, rank_lo, kmin, kmax);
-  scores[row] = (double)(float)((hi - lo) / (double)(rank_hi - rank_lo));
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    const unsigned int a = __shfl_xor_sync(sel.mask, kmin, o), b = __shfl_xor_sync(sel.mask, kmax, o);
+    kmin = a < kmin ? a : kmin;
+    kmax = b > kmax ? b : kmax;
+  }
+  const double hi = sel.sum_smallest(rank_hi, kmin, kmax);
+  const double lo = sel.sum_smallest(rank_lo, kmin, kmax);
+  if (sub == 0) scores[row] = (double)(float)((hi - lo) / (double)(rank_hi - rank_lo));
 }
 
 // ------------------------------------------------------------------ host helpers
@@ -656,12 +688,7 @@ int check_bank_args(long long rows, int channels) {
   return MUSC_B200_OK;
 }
 
-int trimmed_rows_per_block(int n) {
-  const int budget = smem_optin() - 1024;
-  for (int r = 128; r >= 32; r /= 2)
-    if ((long long)n * r * 4 <= budget) return r;
-  return 0;
-}
+int trimmed_pitch(int n) { return n + (((4 - n) % 32) + 32) % 32; }  // >= n, == 4 (mod 32)
 
 }  // namespace
 
@@ -816,13 +843,14 @@ int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, i
 
 int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, int rank_lo, int rank_hi,
                    double* scores, cudaStream_t s) {
-  const int R = trimmed_rows_per_block(n_images);
-  if (R == 0) return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: too many images for shared memory");
-  const size_t smem = (size_t)n_images * R * 4;
+  const int pitch = trimmed_pitch(n_images);
+  const size_t smem = (size_t)kSelRows * pitch * 4;
+  if ((long long)smem > smem_optin() - 1024)
+    return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: too many images for shared memory (N <= ~1700)");
   MUSC_CUDA(cudaFuncSetAttribute(trimmed_mean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const long long blocks = (query_rows + R - 1) / R;
-  trimmed_mean_kernel<<<(unsigned)blocks, R, smem, s>>>(reinterpret_cast<const unsigned int*>(nearest_sq),
-                                                        query_rows, n_images, rank_lo, rank_hi, scores);
+  const long long blocks = (query_rows + kSelRows - 1) / kSelRows;
+  trimmed_mean_kernel<<<(unsigned)blocks, kSelThreads, smem, s>>>(
+      reinterpret_cast<const unsigned int*>(nearest_sq), query_rows, n_images, pitch, rank_lo, rank_hi, scores);
   return check_launch("trimmed_mean_kernel");
 }
 
