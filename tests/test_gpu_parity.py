@@ -217,3 +217,30 @@ def test_msm_is_invariant_to_row_scale_split(cuda_device):
 def test_no_device_timeout_recorded(cuda_device):
     from musc_b200 import _lib
     assert _lib.take_device_error() == _lib.OK
+
+
+def test_trimmed_mean_large_pool(cuda_device):
+    """N = 1024 (config 4): the selection kernel's large-pool shared-memory tile."""
+    from musc_b200 import ops
+    gen = torch.Generator().manual_seed(9)
+    n, rows = 1024, 3000
+    vals = torch.rand(n, rows, generator=gen) + 0.5
+    a, b = ops.trimmed_ranks(n)
+    got = ops.trimmed_mean(vals.to(cuda_device), a, b).cpu().numpy()
+    d = np.sort(np.sqrt(vals.numpy().astype(np.float64)), axis=0)[a:b]
+    np.testing.assert_allclose(got, d.mean(axis=0).astype(np.float32).astype(np.float64), rtol=1e-6, atol=0)
+
+
+def test_super_fast_pipeline_matches_oracle(cuda_device):
+    """Config 3 shape: the super-fast profile through score_pool equals the oracle on the
+    super-fast banks (r = 3, 37x37 -> 28x28, L2-normalised)."""
+    from musc_b200.pipeline import score_pool
+    from musc_b200.synthetic import prototype_mixture_layer
+    n = 12
+    tokens = prototype_mixture_layer(n, generator=torch.Generator().manual_seed(4))
+    res = score_pool([tokens.to(cuda_device)], super_fast_side=28, image_size=64)
+    z = olnamd.l2_normalize(olnamd.lnamd_super_fast(tokens.numpy(), 28))
+    want = omsm.msm(z)
+    np.testing.assert_allclose(res.scores[0, 0].cpu().numpy(), want, rtol=RTOL, atol=0)
+    maps, mx = oreduce.image_scores(want[None, None], 64)
+    np.testing.assert_allclose(res.image_max.cpu().numpy(), mx, rtol=RTOL, atol=0)
