@@ -64,6 +64,7 @@ class VisionEncoder:
                 proj_w=bf(pre + 'mlp.c_proj.weight'), proj_b=f32(pre + 'mlp.c_proj.bias')))
         self.ln_post = (f32('ln_post.weight'), f32('ln_post.bias'))
         self.proj = f32('proj')
+        self._graphs: dict = {}
 
     @classmethod
     def from_reference(cls, visual, device='cuda', compute_dtype=torch.float16) -> 'VisionEncoder':
@@ -79,12 +80,38 @@ class VisionEncoder:
     def _linear(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
         return F.linear(x, w, b.to(self.dtype))
 
-    def forward(self, images: torch.Tensor, out_layers: Sequence[int]):
-        """``images`` (B, 3, H, W) -> ``(pooled (B, out_dim) fp32, [tokens (B, 1+g^2, width) fp32])``."""
+    def forward(self, images: torch.Tensor, out_layers: Sequence[int], graph: bool = True):
+        """``images`` (B, 3, H, W) -> ``(pooled (B, out_dim) fp32, [tokens (B, 1+g^2, width) fp32])``.
+
+        With ``graph`` (CUDA inputs), the first call for a batch shape runs eagerly and
+        captures the whole forward -- GEMMs, LayerNorms and the attention kernel's launches
+        -- into a CUDA graph; later calls copy the images in and replay it.  Outputs are
+        fresh tensors either way.
+        """
         flag = torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction
         torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
         try:
-            return self._forward(images, out_layers)
+            if not graph or not images.is_cuda:
+                return self._forward(images, out_layers)
+            key = (tuple(images.shape), images.dtype, images.device, tuple(int(l) for l in out_layers))
+            entry = self._graphs.get(key)
+            if entry is None:
+                dev = images.device
+                static_in = images.detach().clone()
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):               # warm-up: sets up every launch
+                    out = self._forward(static_in, out_layers)
+                torch.cuda.current_stream(dev).wait_stream(side)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    static_out = self._forward(static_in, out_layers)
+                self._graphs[key] = (g, static_in, static_out)
+                return out
+            g, static_in, (pooled, toks) = entry
+            static_in.copy_(images)
+            g.replay()
+            return pooled.clone(), [t.clone() for t in toks]
         finally:
             torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = flag
 
@@ -103,10 +130,10 @@ class VisionEncoder:
             h = F.layer_norm(x, (w,), *blk['ln_1']).to(lp)
             qkv = self._linear(h, blk['in_w'], blk['in_b'])                      # (B, L, 3w) 16-bit
             a = ops.attention(qkv[..., :w], qkv[..., w:2 * w], qkv[..., 2 * w:], self.heads)
-            x = x + self._linear(a, blk['out_w'], blk['out_b']).float()
+            x = x + self._linear(a, blk['out_w'], blk['out_b'])          # fp32 residual
             h = F.layer_norm(x, (w,), *blk['ln_2']).to(lp)
-            h = F.gelu(self._linear(h, blk['fc_w'], blk['fc_b']).float()).to(lp)
-            x = x + self._linear(h, blk['proj_w'], blk['proj_b']).float()
+            h = F.gelu(self._linear(h, blk['fc_w'], blk['fc_b']))       # evaluated in fp32 by torch
+            x = x + self._linear(h, blk['proj_w'], blk['proj_b'])
             if idx in keep:
                 tokens[idx] = x
         pooled = F.layer_norm(x[:, 0], (w,), *self.ln_post) @ self.proj
