@@ -65,7 +65,7 @@ int musc_b200_take_device_error(int* code);
 int musc_b200_selftest_wait(long long limit_ns, int arrive, musc_b200_stream stream);
 
 /* ------------------------------------------------------------------------
- * LNAMD
+ * LNAMD (models/modules/_LNAMD.py)
  * Replaces LNAMD._embed (models/modules/_LNAMD.py:72-129), its direct-pool
  * form aggregate_features (models/modules/_encoder_gpu.py:14-42) with the
  * radius cache (models/modules/_aggregation_cache.py:15-58), and the
@@ -124,7 +124,7 @@ int musc_b200_lnamd_super_fast(const void* tokens, int dtype, int n_images,
                                musc_b200_stream stream);
 
 /* ------------------------------------------------------------------------
- * MSM mutual scoring
+ * MSM mutual scoring (models/modules/_MSM.py, models/modules/_MSM_gpu.py)
  * Replaces models/modules/_MSM.py:10-59 (original) and
  * models/modules/_MSM_gpu.py:701-830 (the reference GPU driver).
  *
@@ -201,7 +201,7 @@ int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi,
                   musc_b200_stream stream);
 
 /* ------------------------------------------------------------------------
- * Score reduction (SURVEY row a9): models/musc.py:259-288.
+ * Score reduction: models/musc.py:259-288.
  * scores: [n_radii][n_layers][n][side*side] float64.  maps[n][side*side] =
  * mean over layers, then over radii; image_max[n] = max of the bilinear
  * (align_corners=True) up-sampling of each map to image_size^2; upsampled
@@ -212,7 +212,28 @@ int musc_b200_score_maps(const double* scores, int n_radii, int n_layers, int n,
                          musc_b200_stream stream);
 
 /* ------------------------------------------------------------------------
- * Block attention: out = softmax(q k^T * scale) v per
+ * Whole-pool scoring on one GPU (LNAMD, MSM and reduction in one call): the scoring
+ * half of MuSc.make_category_data (models/musc.py:224-288) for non-Python
+ * hosts.  tokens[l] points at layer l's [n_images][tokens_per_image][channels]
+ * tokens (`dtype`).  For every layer: LNAMD of the given radii (one pass,
+ * L2-normalised banks); for every (radius, layer) bank: split-fp16 prep,
+ * symmetric nearest GEMM, interval average over ranks
+ * [int((N-1)*topmin_min), int((N-1)*topmin_max)) (values >= 1 are ranks, as
+ * in models/modules/_MSM_gpu.py:706-709).  Outputs: scores
+ * [n_radii][n_layers][n_images][P] float64, maps [n_images][P] float64 (layer
+ * mean then radius mean) and image_max [n_images] float64 (maximum of the
+ * bilinear align_corners=True up-sampling to image_size^2).
+ * ---------------------------------------------------------------------- */
+size_t musc_b200_score_pool_bytes(int n_images, int tokens_per_image, int channels, int n_radii);
+
+int musc_b200_score_pool(const void* const* tokens, int dtype, int n_images, int tokens_per_image,
+                         int channels, int n_layers, int n_radii, const int* radii, double topmin_min,
+                         double topmin_max, int image_size, double* scores, double* maps,
+                         double* image_max, void* workspace, size_t workspace_bytes,
+                         musc_b200_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Block attention of the ViT-L/14 encoder: out = softmax(q k^T * scale) v per
  * (batch item, head), the core of nn.MultiheadAttention as the reference's ViT
  * blocks call it (models/backbone/open_clip/transformer.py:221-234), with the
  * reference's row-softmax kernel (models/modules/_attention_gpu.py:41-81)

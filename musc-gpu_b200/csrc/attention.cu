@@ -1,4 +1,4 @@
-// Fused block attention: out = softmax(q k^T * scale) v per
+// Fused block attention of the ViT-L/14 encoder: out = softmax(q k^T * scale) v per
 // (batch, head), the core of nn.MultiheadAttention as the reference's ViT
 // blocks call it (models/backbone/open_clip/transformer.py:221-234), with the
 // row softmax the reference moves into its aligned_dual kernel

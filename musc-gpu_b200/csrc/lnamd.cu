@@ -1,4 +1,4 @@
-// LNAMD neighbourhood aggregation.
+// LNAMD neighbourhood aggregation: models/modules/_LNAMD.py and its call in models/musc.py.
 //
 // Reference: LNAMD._embed (models/modules/_LNAMD.py:72-129), its direct-pool
 // form aggregate_features (models/modules/_encoder_gpu.py:14-42), the radius

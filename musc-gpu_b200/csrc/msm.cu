@@ -1,4 +1,4 @@
-// MSM mutual scoring.
+// MSM mutual scoring: models/modules/_MSM.py and models/modules/_MSM_gpu.py.
 //
 // Reference: compute_scores_fast / MSM (models/modules/_MSM.py:10-59) and the
 // reference GPU driver models/modules/_MSM_gpu.py:701-830.

@@ -1,4 +1,4 @@
-// Score reduction (SURVEY row a9): models/musc.py:259-288.
+// Score reduction: models/musc.py:259-288.
 //
 // One CTA per image: the (side*side) map is the mean over layers of each
 // radius's MSM scores, then the mean over radii (float64, models/musc.py:259,

@@ -244,3 +244,33 @@ def test_super_fast_pipeline_matches_oracle(cuda_device):
     np.testing.assert_allclose(res.scores[0, 0].cpu().numpy(), want, rtol=RTOL, atol=0)
     maps, mx = oreduce.image_scores(want[None, None], 64)
     np.testing.assert_allclose(res.image_max.cpu().numpy(), mx, rtol=RTOL, atol=0)
+
+
+def test_c_abi_score_pool_matches_pipeline_and_reference(cuda_device):
+    """musc_b200_score_pool (the one-call C ABI path for non-Python hosts) on config 1:
+    identical to the Python pipeline and within 2e-5 of the reference."""
+    import ctypes
+    from musc_b200 import _lib, ops
+    from musc_b200.pipeline import score_pool
+    from musc_b200.synthetic import prototype_mixture
+    g = golden('pool16')
+    n = int(g['n'])
+    tokens = [t.to(cuda_device) for t in prototype_mixture(n, n_layers=4, c=1024, side=37, seed=int(g['seed']))]
+    lib = _lib.lib()
+    nbytes = lib.musc_b200_score_pool_bytes(n, 1370, 1024, 3)
+    ws = ops._aligned_empty(nbytes, cuda_device)
+    scores = torch.empty(3, 4, n, 1369, dtype=torch.float64, device=cuda_device)
+    maps = torch.empty(n, 1369, dtype=torch.float64, device=cuda_device)
+    mx = torch.empty(n, dtype=torch.float64, device=cuda_device)
+    tok_ptrs = (ctypes.c_void_p * 4)(*[t.data_ptr() for t in tokens])
+    radii = (ctypes.c_int * 3)(1, 3, 5)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    st = lib.musc_b200_score_pool(tok_ptrs, _lib.F32, n, 1370, 1024, 4, 3, radii, 0.0, 0.3, 518,
+                                  ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(maps.data_ptr()),
+                                  ctypes.c_void_p(mx.data_ptr()), ctypes.c_void_p(ws.data_ptr()), nbytes, stream)
+    _lib.check(st, 'musc_b200_score_pool')
+    res = score_pool(tokens)
+    assert torch.equal(scores, res.scores)
+    assert torch.equal(mx, res.image_max)
+    np.testing.assert_allclose(maps.view(n, 37, 37).cpu().numpy(), g['maps'], rtol=RTOL, atol=0)
+    np.testing.assert_allclose(mx.cpu().numpy(), g['image_max'], rtol=RTOL, atol=0)
