@@ -453,10 +453,12 @@ def run_b200(args):
         # original path computes); each rank's launch covers 1/world of the pool's tiles
         msm_flop_per_bank = 2.0 * C * p_score * p_score * pool * (pool - 1)
         achieved_tflops = msm_flop_per_bank / world / (near_avg_ms / 1e3) / 1e12
-        # executed tensor-core work: 3 MMA passes over the symmetric tiles (whole 128 x 256
-        # tiles holding a pair of different images, each pair once), this rank's share
-        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * p_score, p_score, pool) * 128 * 256 * C / world
-                      / (near_avg_ms / 1e3) / 1e12)
+        # executed tensor-core work: 3 MMA passes over the symmetric tiles (whole tiles holding
+        # a pair of different images, each pair once; 256 x 256 for the CTA-pair kernel, 128 x 256
+        # for the single-CTA one), this rank's share
+        tile_m = 256 if os.environ.get('MUSC_B200_NEAREST_PAIR', '1') != '0' else 128
+        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * p_score, p_score, pool, bm=tile_m) * tile_m * 256 * C
+                      / world / (near_avg_ms / 1e3) / 1e12)
         peak = peaks.get('bf16_tflops_sustained', peaks.get('bf16_tflops'))
         line = {
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
@@ -472,7 +474,8 @@ def run_b200(args):
                          'traffic': _traffic() if (args.config == '2' and pool == N_POOL) else None,
                          'peak_kind': f'{peak_kind} bf16 sustained (kernel timed inside a long step)',
                          'mma_executed_tflops': mma_tflops, 'mma_frac': mma_tflops / peak,
-                         'mma_kind': 'kind::f16 (fp16 split hi/lo, 3 passes, symmetric tiles)',
+                         'mma_kind': ('kind::f16 cta_group::%d (fp16 split hi/lo, 3 passes, symmetric %dx256 tiles)'
+                                     % (2 if tile_m == 256 else 1, tile_m)),
                          'launch_ms': near_avg_ms},
             'gpu_launches': launches_timed,
             'clocks': clocks.summary(),

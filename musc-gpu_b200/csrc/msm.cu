@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -97,24 +98,37 @@ prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __ha
 
 // ------------------------------------------------------------------ nearest
 namespace nearest {
-constexpr int BM = 128;           // query rows per tile (TMEM lanes)
+constexpr int CTA_M = 128;        // query rows per CTA (TMEM lanes)
 constexpr int BN = 256;           // reference rows per tile (TMEM columns per accumulator)
 constexpr int BK = 32;            // fp16 elements per K slice = one 64-byte swizzle row
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;                // 8 KB
-constexpr int B_BYTES = BN * BK * 2;                // 16 KB
-constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 48 KB
+constexpr int A_BYTES = CTA_M * BK * 2;  // 8 KB per plane
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr int GROUP_M = 64;  // m-tiles swept together over the reference columns (L2 reuse)
 constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;  // 4 s per wait
-constexpr uint32_t IDESC = tc::idesc_f16(BM, BN, /*fp16*/ 0);
 constexpr float INF = FLT_MAX;
 constexpr int RING = 8;      // tile indices handed from the producer to the MMA and epilogue warps
 constexpr int CHUNK = 8;     // tiles claimed per atomic by the dynamic scheduler
 
+// Tile shapes.  Single CTA: 128 x 256 tiles, the CTA holds all 256 B rows of
+// a K slice.  CTA pair (cta_group::2): 256 x 256 tiles over two SMs; each CTA
+// loads 128 A rows and 128 B rows, so per MMA an SM reads 8 KB of operands
+// from shared memory instead of 12 KB and fetches a third fewer bytes from
+// L2, and the smaller stages allow a 6-deep ring in the same shared memory.
+template <bool PAIR>
+struct Cfg {
+  static constexpr int TILE_M = PAIR ? 256 : 128;
+  static constexpr int CTA_N = PAIR ? 128 : 256;
+  static constexpr int B_BYTES = CTA_N * BK * 2;
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 48 KB / 32 KB
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int GROUP_M = PAIR ? 32 : 64;  // m-tiles swept together (8192 query rows)
+  static constexpr uint32_t IDESC = tc::idesc_f16(TILE_M, BN, /*fp16*/ 0);
+  static constexpr int EPI_ARRIVALS = (PAIR ? 2 : 1) * EPI_WARPS;  // epilogue warps releasing a tile
+};
+
+template <int STAGES, int STAGE_BYTES>
 struct Smem {
   uint8_t tiles[STAGES][STAGE_BYTES];  // 1024-aligned base
   float col_norm[BN];
@@ -130,7 +144,12 @@ struct Smem {
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+template <bool PAIR>
+using SmemT = Smem<Cfg<PAIR>::STAGES, Cfg<PAIR>::STAGE_BYTES>;
+template <bool PAIR>
+constexpr size_t smem_bytes() {
+  return sizeof(SmemT<PAIR>) + 1024;
+}
 
 struct Params {
   const float* q_norm;
@@ -150,18 +169,19 @@ struct Params {
   int num_m, num_n;
 };
 
-__host__ __device__ inline void tile_coords(long long tile, int num_m, int num_n, int* m_blk, int* n_blk) {
-  const long long group = tile / ((long long)GROUP_M * num_n);
-  const int first_m = (int)(group * GROUP_M);
-  const int gm = num_m - first_m < GROUP_M ? num_m - first_m : GROUP_M;
-  const long long local = tile - group * GROUP_M * (long long)num_n;
+__host__ __device__ inline void tile_coords(long long tile, int num_m, int num_n, int group_m, int* m_blk,
+                                            int* n_blk) {
+  const long long group = tile / ((long long)group_m * num_n);
+  const int first_m = (int)(group * group_m);
+  const int gm = num_m - first_m < group_m ? num_m - first_m : group_m;
+  const long long local = tile - group * group_m * (long long)num_n;
   *m_blk = first_m + (int)(local % gm);
   *n_blk = (int)(local / gm);
 }
 
 // Symmetric mode: tile (m, n) holds an element (r, c) with img(r) < img(c).
-__host__ __device__ inline bool sym_needed(int m, int n, long long rows, int patches, int n_images) {
-  const long long r0 = (long long)m * BM;
+__host__ __device__ inline bool sym_needed(int m, int n, long long rows, int patches, int n_images, int tile_m) {
+  const long long r0 = (long long)m * tile_m;
   const long long img_r = r0 / patches;
   if (img_r >= n_images - 1) return false;
   long long c_last = (long long)n * BN + BN - 1;
@@ -170,19 +190,24 @@ __host__ __device__ inline bool sym_needed(int m, int n, long long rows, int pat
 }
 
 // Bounded wait: true when the phase completed; false after the time limit
-// (which raises the CTA's abort flag and the device error word) or when
-// another role already aborted.
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                             int* err) {
-  if (tc::mbar_try_wait(bar, parity)) return true;
+// (which raises this CTA's abort flag, the peer CTA's when `peer_abort` is a
+// cluster address, and the device error word) or when an abort was already
+// raised.  CLUSTER selects acquire at cluster scope, for phases completed by
+// the other CTA of a pair.
+template <bool CLUSTER>
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                             uint32_t peer_abort) {
+  auto ready = [&]() { return CLUSTER ? tc::mbar_try_wait_cluster(bar, parity) : tc::mbar_try_wait(bar, parity); };
+  if (ready()) return true;
   const uint64_t start = global_ns();
   uint32_t iter = 0;
   while (true) {
-    if (tc::mbar_try_wait(bar, parity)) return true;
+    if (ready()) return true;
     if ((++iter & 255u) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - start > WAIT_LIMIT_NS) {
         *abort_flag = 1;
+        if (peer_abort) tc::st_cluster_u32(peer_abort, 1u);
         atomicExch(err, MUSC_B200_ERR_TIMEOUT);
         return false;
       }
@@ -239,30 +264,42 @@ __device__ __forceinline__ float warp_column_min(float (&v)[32], int lane) {
   return v[0];
 }
 
-template <bool SYM>
+// Roles (one CTA, or each CTA of a pair): warp 0 lane 0 loads (TMA), warp 1
+// lane 0 issues the MMAs (the even CTA only, for a pair), warps 2-5 are the
+// epilogue.  In a pair the even CTA (rank 0) owns the schedule: its producer
+// claims each tile, writes the index into both CTAs' rings and both CTAs'
+// loads complete on its `full` barriers; its MMA thread signals both CTAs'
+// `empty` and `acc_full` barriers; both epilogues release the accumulator and
+// the ring slot on its barriers.
+template <bool SYM, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
 nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_constant__ CUtensorMap map_q_lo,
                const __grid_constant__ CUtensorMap map_r_hi, const __grid_constant__ CUtensorMap map_r_lo,
                const Params p) {
+  using C = Cfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SmemT<PAIR>& sm =
+      *reinterpret_cast<SmemT<PAIR>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &sm.abort_flag;
+  const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const uint32_t peer_abort = PAIR ? tc::mapa(tc::smem_u32(&sm.abort_flag), rank ^ 1u) : 0u;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       tc::mbar_init(tc::smem_u32(&sm.full[s]), 1);
       tc::mbar_init(tc::smem_u32(&sm.empty[s]), 1);
     }
     for (int a = 0; a < NUM_ACC; ++a) {
       tc::mbar_init(tc::smem_u32(&sm.acc_full[a]), 1);
-      tc::mbar_init(tc::smem_u32(&sm.acc_empty[a]), EPI_WARPS);
+      tc::mbar_init(tc::smem_u32(&sm.acc_empty[a]), C::EPI_ARRIVALS);
     }
     tc::mbar_init(tc::smem_u32(&sm.drain), 1);
     for (int i = 0; i < RING; ++i) {
       tc::mbar_init(tc::smem_u32(&sm.ring_full[i]), 1);
-      tc::mbar_init(tc::smem_u32(&sm.ring_empty[i]), EPI_WARPS);
+      tc::mbar_init(tc::smem_u32(&sm.ring_empty[i]), C::EPI_ARRIVALS);
     }
     sm.abort_flag = 0;
     tc::fence_barrier_init();
@@ -272,11 +309,17 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
     tc::prefetch_tensormap(&map_r_lo);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
-    tc::tmem_relinquish();
+    if (PAIR) {
+      tc::tmem_alloc_pair(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
+  if (PAIR) tc::cluster_sync();  // the peer's barriers exist before anything arrives on them
   tc::fence_after_sync();
   const uint32_t tmem_base = sm.tmem_base;
 
@@ -285,12 +328,14 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_phase[STAGES];
-      bool issued[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
+      uint32_t issued_phase[C::STAGES];
+      bool issued[C::STAGES];
+      for (int s = 0; s < C::STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
       bool ok = true;
-      long long next_static = p.tile_begin + blockIdx.x, chunk_cur = 0, chunk_end = 0;
-      // Next tile this CTA evaluates (linear index), or -1.  Static: stride gridDim.x.
+      const long long group_id = PAIR ? (long long)tc::cluster_id_x() : (long long)blockIdx.x;
+      const long long n_groups = PAIR ? (long long)tc::cluster_count_x() : (long long)gridDim.x;
+      long long next_static = p.tile_begin + group_id, chunk_cur = 0, chunk_end = 0;
+      // Next tile (linear index), or -1.  Static: stride = number of CTAs (pairs).
       // Dynamic: claim CHUNK consecutive indices per atomic, so CTAs that start late
       // (their SM busy with another kernel, e.g. a collective) simply take fewer.
       auto next_tile = [&]() -> long long {
@@ -307,59 +352,92 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
           } else {
             t = next_static;
             if (t >= p.tile_end) return -1;
-            next_static += gridDim.x;
+            next_static += n_groups;
           }
           if (!SYM) return t;
           int mb, nb;
-          tile_coords(t, p.num_m, p.num_n, &mb, &nb);
-          if (sym_needed(mb, nb, p.r_rows, p.patches, p.n_images)) return t;
+          tile_coords(t, p.num_m, p.num_n, C::GROUP_M, &mb, &nb);
+          if (sym_needed(mb, nb, p.r_rows, p.patches, p.n_images, C::TILE_M)) return t;
         }
       };
       for (int local = 0; ok; ++local) {
         const int slot = local % RING;
-        if (!wait_bounded(tc::smem_u32(&sm.ring_empty[slot]), ((uint32_t)(local / RING) & 1u) ^ 1u,
-                          abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
-        const long long tile = next_tile();
-        sm.tile_ring[slot] = tile;
-        tc::mbar_arrive(tc::smem_u32(&sm.ring_full[slot]));
-        if (tile < 0) break;
-        int m_blk, n_blk;
-        tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bounded(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err)) {
+        const uint32_t ring_parity = (uint32_t)(local / RING) & 1u;
+        long long tile;
+        if (leader) {
+          if (!wait_bounded<PAIR>(tc::smem_u32(&sm.ring_empty[slot]), ring_parity ^ 1u, abort_flag, p.err,
+                                  peer_abort)) {
             ok = false;
             break;
           }
-          const uint32_t full = tc::smem_u32(&sm.full[stage]);
-          tc::mbar_arrive_expect_tx(full, STAGE_BYTES);
+          tile = next_tile();
+          sm.tile_ring[slot] = tile;
+          if (PAIR) {
+            tc::st_cluster_s64(tc::mapa(tc::smem_u32(&sm.tile_ring[slot]), 1u), tile);
+            tc::mbar_arrive_cluster(tc::mapa(tc::smem_u32(&sm.ring_full[slot]), 1u));
+          }
+          tc::mbar_arrive(tc::smem_u32(&sm.ring_full[slot]));
+        } else {
+          if (!wait_bounded<true>(tc::smem_u32(&sm.ring_full[slot]), ring_parity, abort_flag, p.err, peer_abort)) {
+            ok = false;
+            break;
+          }
+          tile = sm.tile_ring[slot];
+        }
+        if (tile < 0) break;
+        int m_blk, n_blk;
+        tile_coords(tile, p.num_m, p.num_n, C::GROUP_M, &m_blk, &n_blk);
+        const int a_row = m_blk * C::TILE_M + (int)rank * CTA_M;
+        const int b_row = n_blk * BN + (int)rank * C::CTA_N;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!wait_bounded<false>(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err, peer_abort)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_local = tc::smem_u32(&sm.full[stage]);
+          // The leader's barrier counts both CTAs' bytes of this stage.
+          if (leader) tc::mbar_arrive_expect_tx(full_local, (PAIR ? 2 : 1) * C::STAGE_BYTES);
           const uint32_t base = tc::smem_u32(sm.tiles[stage]);
           const int kc = kb * BK;
-          tc::tma_load_2d(base, &map_q_hi, kc, m_blk * BM, full);
-          tc::tma_load_2d(base + A_BYTES, &map_q_lo, kc, m_blk * BM, full);
-          tc::tma_load_2d(base + 2 * A_BYTES, &map_r_hi, kc, n_blk * BN, full);
-          tc::tma_load_2d(base + 2 * A_BYTES + B_BYTES, &map_r_lo, kc, n_blk * BN, full);
+          if (PAIR) {
+            const uint32_t full = tc::mapa(full_local, 0u);
+            tc::tma_load_2d_pair(base, &map_q_hi, kc, a_row, full);
+            tc::tma_load_2d_pair(base + A_BYTES, &map_q_lo, kc, a_row, full);
+            tc::tma_load_2d_pair(base + 2 * A_BYTES, &map_r_hi, kc, b_row, full);
+            tc::tma_load_2d_pair(base + 2 * A_BYTES + C::B_BYTES, &map_r_lo, kc, b_row, full);
+          } else {
+            tc::tma_load_2d(base, &map_q_hi, kc, a_row, full_local);
+            tc::tma_load_2d(base + A_BYTES, &map_q_lo, kc, a_row, full_local);
+            tc::tma_load_2d(base + 2 * A_BYTES, &map_r_hi, kc, b_row, full_local);
+            tc::tma_load_2d(base + 2 * A_BYTES + C::B_BYTES, &map_r_lo, kc, b_row, full_local);
+          }
           issued[stage] = true;
           issued_phase[stage] = phase;
-          if (++stage == STAGES) stage = 0, phase ^= 1;
+          if (++stage == C::STAGES) stage = 0, phase ^= 1;
         }
       }
       if (!ok) {
-        // Let the copies already in flight land before the CTA exits.
-        for (int s = 0; s < STAGES; ++s) {
-          if (!issued[s]) continue;
-          const uint64_t start = global_ns();
-          while (!tc::mbar_try_wait(tc::smem_u32(&sm.full[s]), issued_phase[s]) &&
-                 global_ns() - start < WAIT_LIMIT_NS) {
+        // Let the copies already in flight land before the CTA exits.  The
+        // leader watches its `full` barriers (one deadline for all stages); the
+        // peer's copies complete on the leader's barriers, so it gives them a
+        // fixed 2 ms, far above the latency of one copy.
+        const uint64_t start = global_ns();
+        if (leader) {
+          for (int s = 0; s < C::STAGES; ++s) {
+            if (!issued[s]) continue;
+            while (!tc::mbar_try_wait(tc::smem_u32(&sm.full[s]), issued_phase[s]) &&
+                   global_ns() - start < WAIT_LIMIT_NS) {
+            }
+          }
+        } else {
+          while (global_ns() - start < 2000000ull) {
           }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -367,20 +445,20 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       bool ok = true;
       for (int local = 0; ok; ++local) {
         const int slot = local % RING;
-        if (!wait_bounded(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u, abort_flag,
-                          p.err)) {
+        if (!wait_bounded<false>(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u, abort_flag,
+                                 p.err, peer_abort)) {
           ok = false;
           break;
         }
         if (sm.tile_ring[slot] < 0) break;
-        if (!wait_bounded(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err)) {
+        if (!wait_bounded<PAIR>(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, peer_abort)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bounded(tc::smem_u32(&sm.full[stage]), phase, abort_flag, p.err)) {
+          if (!wait_bounded<false>(tc::smem_u32(&sm.full[stage]), phase, abort_flag, p.err, peer_abort)) {
             ok = false;
             break;
           }
@@ -392,21 +470,41 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
             const uint64_t a_hi = tc::desc_k_sw64(base + koff);
             const uint64_t a_lo = tc::desc_k_sw64(base + A_BYTES + koff);
             const uint64_t b_hi = tc::desc_k_sw64(base + 2 * A_BYTES + koff);
-            const uint64_t b_lo = tc::desc_k_sw64(base + 2 * A_BYTES + B_BYTES + koff);
-            tc::mma_f16_ss(d_tmem, a_hi, b_hi, IDESC, (kb | k16) != 0 ? 1u : 0u);
-            tc::mma_f16_ss(d_tmem, a_hi, b_lo, IDESC, 1u);
-            tc::mma_f16_ss(d_tmem, a_lo, b_hi, IDESC, 1u);
+            const uint64_t b_lo = tc::desc_k_sw64(base + 2 * A_BYTES + C::B_BYTES + koff);
+            const uint32_t first = (kb | k16) != 0 ? 1u : 0u;
+            if (PAIR) {
+              tc::mma_f16_ss_pair(d_tmem, a_hi, b_hi, C::IDESC, first);
+              tc::mma_f16_ss_pair(d_tmem, a_hi, b_lo, C::IDESC, 1u);
+              tc::mma_f16_ss_pair(d_tmem, a_lo, b_hi, C::IDESC, 1u);
+            } else {
+              tc::mma_f16_ss(d_tmem, a_hi, b_hi, C::IDESC, first);
+              tc::mma_f16_ss(d_tmem, a_hi, b_lo, C::IDESC, 1u);
+              tc::mma_f16_ss(d_tmem, a_lo, b_hi, C::IDESC, 1u);
+            }
           }
-          tc::mma_commit(tc::smem_u32(&sm.empty[stage]));
-          if (++stage == STAGES) stage = 0, phase ^= 1;
+          const uint32_t empty = tc::smem_u32(&sm.empty[stage]);
+          if (PAIR) {
+            tc::mma_commit_pair(empty);
+            tc::mma_commit_pair(tc::mapa(empty, 1u));
+          } else {
+            tc::mma_commit(empty);
+          }
+          if (++stage == C::STAGES) stage = 0, phase ^= 1;
         }
         if (!ok) break;
-        tc::mma_commit(tc::smem_u32(&sm.acc_full[acc]));
+        const uint32_t accf = tc::smem_u32(&sm.acc_full[acc]);
+        if (PAIR) {
+          tc::mma_commit_pair(accf);
+          tc::mma_commit_pair(tc::mapa(accf, 1u));
+        } else {
+          tc::mma_commit(accf);
+        }
         if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
       }
       if (!ok) {
         // Wait for this thread's MMAs in flight before TMEM is released.
-        tc::mma_commit(tc::smem_u32(&sm.drain));
+        if (PAIR) tc::mma_commit_pair(tc::smem_u32(&sm.drain));
+        else tc::mma_commit(tc::smem_u32(&sm.drain));
         const uint64_t start = global_ns();
         while (!tc::mbar_try_wait(tc::smem_u32(&sm.drain), 0) && global_ns() - start < WAIT_LIMIT_NS) {
         }
@@ -421,12 +519,12 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
     uint32_t acc_phase = 0;
     for (int local = 0;; ++local) {
       const int slot = local % RING;
-      const bool got = wait_bounded(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u,
-                                    abort_flag, p.err);
+      const bool got = wait_bounded<PAIR>(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u,
+                                          abort_flag, p.err, peer_abort);
       const long long tile = got ? sm.tile_ring[slot] : -1;
       if (named_sync_epi_any(tile < 0)) break;  // uniform: every epilogue thread read the same slot
       int m_blk, n_blk;
-      tile_coords(tile, p.num_m, p.num_n, &m_blk, &n_blk);
+      tile_coords(tile, p.num_m, p.num_n, C::GROUP_M, &m_blk, &n_blk);
       const long long n0 = (long long)n_blk * BN;
       named_sync_epi();  // previous tile's readers are done with col_norm / col_w
       for (int j = et; j < BN; j += EPI_WARPS * 32) {
@@ -435,11 +533,12 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
         sm.col_norm[j] = ok ? __ldg(p.r_norm + col) : 0.f;
         sm.col_w[j] = ok ? 2.f * __ldg(p.r_inv + col) : 0.f;
       }
-      wait_bounded(tc::smem_u32(&sm.acc_full[acc]), acc_phase, abort_flag, p.err);
+      wait_bounded<false>(tc::smem_u32(&sm.acc_full[acc]), acc_phase, abort_flag, p.err, peer_abort);
       if (named_sync_epi_any(*abort_flag)) break;  // uniform decision across the epilogue warps
       tc::fence_after_sync();
 
-      const long long warp_row0 = (long long)m_blk * BM + quarter * 32;
+      const long long cta_row0 = (long long)m_blk * C::TILE_M + (long long)rank * CTA_M;
+      const long long warp_row0 = cta_row0 + quarter * 32;
       const long long row = warp_row0 + lane;
       const bool row_ok = row < p.q_rows;
       const float qn = row_ok ? __ldg(p.q_norm + row) : 0.f;
@@ -447,10 +546,10 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       const int q_img = (int)((p.q_first_row + row) / P);
       // Symmetric mode keeps only columns of a later image than the row's.
       const long long col_from = SYM ? (long long)(q_img + 1) * P : 0;
-      long long tile_last_row = (long long)m_blk * BM + BM - 1;
-      if (tile_last_row > p.q_rows - 1) tile_last_row = p.q_rows - 1;
-      const bool rows_full = (long long)m_blk * BM + BM <= p.q_rows;
-      const bool clean = !SYM || (rows_full && (tile_last_row / P) < (n0 / P));
+      long long cta_last_row = cta_row0 + CTA_M - 1;
+      if (cta_last_row > p.q_rows - 1) cta_last_row = p.q_rows - 1;
+      const bool rows_full = cta_row0 + CTA_M <= p.q_rows;
+      const bool clean = !SYM || (rows_full && (cta_last_row / P) < (n0 / P));
       // row images covered by this warp (symmetric column minima)
       const bool warp_any = warp_row0 < p.q_rows;
       long long warp_last = warp_row0 + 31;
@@ -522,8 +621,15 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) {
-        tc::mbar_arrive(tc::smem_u32(&sm.acc_empty[acc]));
-        tc::mbar_arrive(tc::smem_u32(&sm.ring_empty[slot]));
+        const uint32_t acc_e = tc::smem_u32(&sm.acc_empty[acc]);
+        const uint32_t ring_e = tc::smem_u32(&sm.ring_empty[slot]);
+        if (leader) {
+          tc::mbar_arrive(acc_e);
+          tc::mbar_arrive(ring_e);
+        } else {
+          tc::mbar_arrive_cluster(tc::mapa(acc_e, 0u));
+          tc::mbar_arrive_cluster(tc::mapa(ring_e, 0u));
+        }
       }
       if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
     }
@@ -531,10 +637,13 @@ nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_consta
 
   tc::fence_before_sync();
   __syncthreads();
+  if (PAIR) tc::cluster_sync();  // no access to the other CTA's shared memory or TMEM is still pending
   if (warp == 1) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tc::tmem_dealloc(tmem_base, TMEM_COLS);
   }
+  if (PAIR) tc::cluster_sync();
 }
 
 }  // namespace nearest
@@ -698,12 +807,13 @@ int trimmed_pitch(int n) { return n + (((4 - n) % 32) + 32) % 32; }  // >= n, ==
 // n_start(m), the first n-tile holding a column of a later image than the
 // m-tile's first row.  Part k starts at the first column whose preceding
 // count reaches total * k / parts.
-static void sym_part_range(long long rows, int patches, int n_images, int num_m, int num_n, int part,
-                           int parts, long long* tile_begin, long long* tile_end) {
-  using namespace nearest;
+static void sym_part_range(long long rows, int patches, int n_images, int num_m, int num_n, int tile_m,
+                           int group_m, int part, int parts, long long* tile_begin, long long* tile_end) {
+  using nearest::BN;
+  const int GROUP_M = group_m;
   std::vector<int> n_start(num_m);
   for (int m = 0; m < num_m; ++m) {
-    const long long img = (long long)m * BM / patches;
+    const long long img = (long long)m * tile_m / patches;
     if (img >= n_images - 1) {
       n_start[m] = num_n;
     } else {
@@ -743,13 +853,23 @@ static int set_smem_attr() {
   MUSC_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lock(m);
   if (dev >= 64 || !done[dev]) {
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)nearest::SMEM_BYTES));
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)nearest::SMEM_BYTES));
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<false, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<false>()));
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<false>()));
+    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true, true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<true>()));
     if (dev < 64) done[dev] = true;
   }
   return MUSC_B200_OK;
+}
+
+// The symmetric pool kernel runs as CTA pairs (cta_group::2) unless
+// MUSC_B200_NEAREST_PAIR=0 selects the single-CTA kernel; both compute the
+// same table bit for bit.
+static bool use_cta_pairs() {
+  const char* e = std::getenv("MUSC_B200_NEAREST_PAIR");
+  return !(e && e[0] == '0');
 }
 
 static int fill_table(float* table, long long count, cudaStream_t s) {
@@ -765,8 +885,8 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   const uint8_t* qb = static_cast<const uint8_t*>(query_bank);
   const uint8_t* rb = static_cast<const uint8_t*>(ref_bank);
   CUtensorMap mqh, mql, mrh, mrl;
-  MUSC_TRY(make_plane_map(&mqh, qb + ql.hi, query_rows, channels, nearest::BM));
-  MUSC_TRY(make_plane_map(&mql, qb + ql.lo, query_rows, channels, nearest::BM));
+  MUSC_TRY(make_plane_map(&mqh, qb + ql.hi, query_rows, channels, nearest::CTA_M));
+  MUSC_TRY(make_plane_map(&mql, qb + ql.lo, query_rows, channels, nearest::CTA_M));
   MUSC_TRY(make_plane_map(&mrh, rb + rl.hi, ref_rows, channels, nearest::BN));
   MUSC_TRY(make_plane_map(&mrl, rb + rl.lo, ref_rows, channels, nearest::BN));
   const int n_images = (int)(ref_rows / patches);
@@ -787,14 +907,15 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   p.patches = patches;
   p.n_images = n_images;
   p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
-  p.num_m = (int)((query_rows + nearest::BM - 1) / nearest::BM);
+  p.num_m = (int)((query_rows + nearest::CTA_M - 1) / nearest::CTA_M);
   p.num_n = (int)((ref_rows + nearest::BN - 1) / nearest::BN);
   p.tile_begin = 0;
   p.tile_end = (long long)p.num_m * p.num_n;
   p.sched = nullptr;  // static schedule
   MUSC_TRY(set_smem_attr());
   const int grid = (int)std::min<long long>(p.tile_end, sm_count());
-  nearest::nearest_kernel<false><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mqh, mql, mrh, mrl, p);
+  nearest::nearest_kernel<false, false><<<grid, nearest::THREADS, nearest::smem_bytes<false>(), s>>>(
+      mqh, mql, mrh, mrl, p);
   return check_launch("nearest_kernel<directed>");
 }
 
@@ -803,11 +924,13 @@ int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, i
                         cudaStream_t s) {
   const BankLayout l = bank_layout(bank_rows, channels);
   const uint8_t* b = static_cast<const uint8_t*>(bank);
+  const bool pair = use_cta_pairs();
+  const int b_box = pair ? nearest::Cfg<true>::CTA_N : nearest::Cfg<false>::CTA_N;
   CUtensorMap mah, mal, mbh, mbl;
-  MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, nearest::BM));
-  MUSC_TRY(make_plane_map(&mal, b + l.lo, rows, channels, nearest::BM));
-  MUSC_TRY(make_plane_map(&mbh, b + l.hi, rows, channels, nearest::BN));
-  MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, nearest::BN));
+  MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, nearest::CTA_M));
+  MUSC_TRY(make_plane_map(&mal, b + l.lo, rows, channels, nearest::CTA_M));
+  MUSC_TRY(make_plane_map(&mbh, b + l.hi, rows, channels, b_box));
+  MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, b_box));
   const int n_images = (int)(rows / patches);
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
   const long long table = blocks * n_images * rows_per_block;
@@ -830,15 +953,41 @@ int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, i
   p.patches = patches;
   p.n_images = n_images;
   p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
-  p.num_m = (int)((rows + nearest::BM - 1) / nearest::BM);
+  const int tile_m = pair ? nearest::Cfg<true>::TILE_M : nearest::Cfg<false>::TILE_M;
+  const int group_m = pair ? nearest::Cfg<true>::GROUP_M : nearest::Cfg<false>::GROUP_M;
+  p.num_m = (int)((rows + tile_m - 1) / tile_m);
   p.num_n = (int)((rows + nearest::BN - 1) / nearest::BN);
-  sym_part_range(rows, patches, n_images, p.num_m, p.num_n, part, parts, &p.tile_begin, &p.tile_end);
+  sym_part_range(rows, patches, n_images, p.num_m, p.num_n, tile_m, group_m, part, parts, &p.tile_begin,
+                 &p.tile_end);
   if (p.tile_end <= p.tile_begin) return MUSC_B200_OK;  // nothing to do for this part
   MUSC_TRY(set_smem_attr());
   const int sms = sm_count();
-  const int grid = max_ctas > 0 && max_ctas < sms ? max_ctas : sms;
-  nearest::nearest_kernel<true><<<grid, nearest::THREADS, nearest::SMEM_BYTES, s>>>(mah, mal, mbh, mbl, p);
-  return check_launch("nearest_kernel<symmetric>");
+  const int ctas = max_ctas > 0 && max_ctas < sms ? max_ctas : sms;
+  if (!pair) {
+    nearest::nearest_kernel<true, false><<<ctas, nearest::THREADS, nearest::smem_bytes<false>(), s>>>(
+        mah, mal, mbh, mbl, p);
+    return check_launch("nearest_kernel<symmetric>");
+  }
+  // One cluster of two CTAs per SM pair, as many as can be resident at once.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(nearest::THREADS);
+  cfg.dynamicSmemBytes = nearest::smem_bytes<true>();
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  MUSC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, nearest::nearest_kernel<true, true>, &cfg));
+  if (clusters <= 0) return fail(MUSC_B200_ERR_CUDA, "nearest_pool: no CTA pair fits on this device");
+  clusters = std::min(clusters, std::max(1, ctas / 2));
+  cfg.gridDim = dim3(2 * clusters);
+  MUSC_CUDA(cudaLaunchKernelEx(&cfg, nearest::nearest_kernel<true, true>, mah, mal, mbh, mbl, p));
+  return check_launch("nearest_kernel<symmetric, pair>");
 }
 
 int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, int rank_lo, int rank_hi,

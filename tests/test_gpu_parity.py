@@ -147,6 +147,35 @@ def test_symmetric_parts_combine_exactly(cuda_device, parts):
     assert torch.equal(flat, whole)
 
 
+@pytest.mark.parametrize('n,p,c,parts,max_ctas', [(2, 196, 64, 1, 0), (13, 1369, 64, 1, 0),
+                                                    (13, 1369, 64, 3, 0), (9, 1369, 1024, 2, 0),
+                                                    (7, 1369, 256, 1, 5)])
+def test_cta_pair_kernel_equals_single_cta(cuda_device, monkeypatch, n, p, c, parts, max_ctas):
+    """The CTA-pair pool kernel (cta_group::2, 256 x 256 tiles over two SMs) and the single-CTA
+    kernel (128 x 256 tiles) give the same MIN-combined table bit for bit: row counts that are
+    not a multiple of 256, N = 2, per-rank parts in the blocked layout, an odd CTA cap."""
+    from musc_b200 import ops
+    from musc_b200.pipeline import shard_range
+    z = torch.randn(n * p, c, generator=torch.Generator().manual_seed(n * 7 + parts)).to(cuda_device)
+    bank = ops.prep_bank(z)
+    rpb = shard_range(n, parts, 0)[2] * p
+    tables = {}
+    for pair in ('0', '1'):
+        monkeypatch.setenv('MUSC_B200_NEAREST_PAIR', pair)
+        combined = None
+        for k in range(parts):
+            t = ops.nearest_pool(bank, n * p, c, p, k, parts, rpb, max_ctas=max_ctas).clone()
+            combined = t if combined is None else torch.minimum(combined, t)
+        tables[pair] = combined
+    assert torch.equal(tables['0'], tables['1'])
+    assert _lib_device_error_clear()
+
+
+def _lib_device_error_clear() -> bool:
+    from musc_b200 import _lib
+    return _lib.take_device_error() == _lib.OK
+
+
 def test_trimmed_mean_ties_and_offsets(cuda_device):
     from musc_b200 import ops
     gen = torch.Generator().manual_seed(5)
