@@ -338,9 +338,15 @@ def run_b200(args):
         return [torch.cat(t) if t else torch.empty(0, 1 + P, C, device=dev) for t in layers]
 
     def step(inputs, ready=None):
-        return pipeline.score_pool(tokens_of(inputs), n_images=pool, radii=radii, group=group, kernels=kern,
-                                   super_fast_side=sf, ready=None if encoder is not None else ready,
-                                   collective_sms=args.collective_sms)
+        # NVTX range "pool_step": lets a profiler capture the launches of the pool steps only
+        # (ncu --nvtx --nvtx-include "pool_step/"), not the synthetic-input generation
+        torch.cuda.nvtx.range_push('pool_step')
+        try:
+            return pipeline.score_pool(tokens_of(inputs), n_images=pool, radii=radii, group=group, kernels=kern,
+                                       super_fast_side=sf, ready=None if encoder is not None else ready,
+                                       collective_sms=args.collective_sms)
+        finally:
+            torch.cuda.nvtx.range_pop()
 
     def barrier():
         if group is not None:

@@ -22,7 +22,9 @@
 // statistics, the same again for the stencil, and n_radii * n * P * C * 4
 // written.
 #include "common.cuh"
+#include "tc.cuh"
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -88,7 +90,11 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
 __device__ __forceinline__ float4 f4scale(float4 a, float s) {
   return make_float4(a.x * s, a.y * s, a.z * s, a.w * s);
 }
-__device__ __forceinline__ float f4dot(float4 a) { return a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w; }
+// Explicit FMA chain: nothing left for the compiler to contract, so every
+// kernel that uses it rounds identically.
+__device__ __forceinline__ float f4dot(float4 a) {
+  return __fmaf_rn(a.w, a.w, __fmaf_rn(a.z, a.z, __fmaf_rn(a.y, a.y, __fmul_rn(a.x, a.x))));
+}
 
 // Block-wide sum of up to three values; `buf` alternates between calls so a
 // single __syncthreads per call suffices.  Every thread gets the totals.
@@ -181,6 +187,142 @@ lnamd_stencil_kernel(const T* __restrict__ tokens, int tokens_per_image, int cha
       if (want1) *reinterpret_cast<float4*>(o1p + off) = o1;
       if (want3) *reinterpret_cast<float4*>(o3p + off) = o3;
       if (want5) *reinterpret_cast<float4*>(o5p + off) = o5;
+    }
+  }
+}
+
+// Staged form of lnamd_stencil_kernel with the same arithmetic in the same
+// order (bit-identical outputs).  Thread 0 streams the (up to five) input
+// tokens of each column into a kBulkDepth-deep shared-memory ring with untiled
+// bulk copies, kBulkDepth columns ahead, so every CTA keeps its next columns'
+// reads in flight without holding them in registers (which lets three
+// 256-thread CTAs share an SM); the other threads read their four channels
+// from shared memory.  One __syncthreads per column (the L2-norm reduction's)
+// frees the column's slot for the next copy.  Requires channels * sizeof(T)
+// % 16 == 0 (bulk-copy granularity).
+constexpr uint64_t kBulkWaitNs = 2000000000ull;  // 2 s per column
+
+template <typename T, int kBulkDepth, int kThreads, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
+lnamd_stencil_bulk_kernel(const T* __restrict__ tokens, int tokens_per_image, int channels, int side,
+                          const double* __restrict__ partial, float* out1, float* out3, float* out5,
+                          long long out_image_stride, long long out_patch_stride, int normalize, int* err) {
+  extern __shared__ __align__(128) uint8_t ring_raw[];  // [kBulkDepth][5][channels] of T
+  __shared__ float red[2 * 32 * 3];
+  __shared__ __align__(8) uint64_t full[kBulkDepth];
+  __shared__ int aborted;
+  const T* ring = reinterpret_cast<const T*>(ring_raw);
+  const int y = blockIdx.x;
+  const int img = blockIdx.y;
+  const int cg = threadIdx.x;  // channel group of 4
+  const bool active = cg * 4 < channels;
+  const uint32_t row_bytes = (uint32_t)channels * (uint32_t)sizeof(T);
+  const T* body = tokens + (long long)img * tokens_per_image * channels + channels;
+  const int y_lo = y - 2 < 0 ? 0 : y - 2;
+  const int y_hi = y + 2 > side - 1 ? side - 1 : y + 2;
+  const uint32_t col_bytes = (uint32_t)(y_hi - y_lo + 1) * row_bytes;
+
+  auto issue = [&](int xc) {  // thread 0: column xc into slot xc % kBulkDepth
+    const int slot = xc % kBulkDepth;
+    const uint32_t bar = tc::smem_u32(&full[slot]);
+    tc::mbar_arrive_expect_tx(bar, col_bytes);
+    for (int yy = y_lo; yy <= y_hi; ++yy) {
+      const uint32_t dst = tc::smem_u32(ring_raw + ((size_t)slot * 5 + (yy - y + 2)) * row_bytes);
+      tc::bulk_load(dst, body + ((long long)yy * side + xc) * channels, row_bytes, bar);
+    }
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkDepth; ++s) tc::mbar_init(tc::smem_u32(&full[s]), 1);
+    aborted = 0;
+    tc::fence_barrier_init();
+    for (int xc = 0; xc < kBulkDepth && xc < side; ++xc) issue(xc);
+  }
+  float mu, rstd;
+  image_moments(partial, img, (double)side * side * channels, &mu, &rstd);
+  __syncthreads();
+
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 a1[3] = {zero, zero, zero};        // V1 at x'-2 .. x'
+  float4 a3[4] = {zero, zero, zero, zero};  // V3 at x'-3 .. x'
+  float4 a5[5] = {zero, zero, zero, zero, zero};
+  const bool want1 = out1 != nullptr, want3 = out3 != nullptr, want5 = out5 != nullptr;
+  const float s1 = rstd, s3 = rstd / 9.f, s5 = rstd / 25.f;
+  float* o1p = want1 ? out1 + (long long)img * out_image_stride + cg * 4 : nullptr;
+  float* o3p = want3 ? out3 + (long long)img * out_image_stride + cg * 4 : nullptr;
+  float* o5p = want5 ? out5 + (long long)img * out_image_stride + cg * 4 : nullptr;
+
+  for (int xp = 0; xp < side + 2; ++xp) {
+    float4 cur[5];
+    if (xp < side) {
+      const int slot = xp % kBulkDepth;
+      const uint32_t bar = tc::smem_u32(&full[slot]);
+      const uint32_t parity = (uint32_t)(xp / kBulkDepth) & 1u;
+      if (!tc::mbar_try_wait(bar, parity)) {
+        const uint64_t start = global_ns();
+        while (!tc::mbar_try_wait(bar, parity)) {
+          if (*reinterpret_cast<volatile int*>(&aborted)) break;
+          if (global_ns() - start > kBulkWaitNs) {
+            aborted = 1;
+            atomicExch(err, MUSC_B200_ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < 5; ++d) {
+        const int yy = y + d - 2;
+        if (active && yy >= 0 && yy < side) {
+          const float4 t = load4_shared(ring + ((size_t)slot * 5 + d) * channels + cg * 4);
+          cur[d] = make_float4(t.x - mu, t.y - mu, t.z - mu, t.w - mu);
+        } else {
+          cur[d] = zero;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < 5; ++d) cur[d] = zero;
+    }
+    const float4 v1 = cur[2];
+    const float4 v3 = f4add(f4add(cur[1], cur[2]), cur[3]);
+    const float4 v5 = f4add(f4add(v3, cur[0]), cur[4]);
+    a1[0] = a1[1]; a1[1] = a1[2]; a1[2] = v1;
+    a3[0] = a3[1]; a3[1] = a3[2]; a3[2] = a3[3]; a3[3] = v3;
+    a5[0] = a5[1]; a5[1] = a5[2]; a5[2] = a5[3]; a5[3] = a5[4]; a5[4] = v5;
+    const int x = xp - 2;
+    float4 o1 = zero, o3 = zero, o5 = zero;
+    if (x >= 0) {
+      o1 = f4scale(a1[0], s1);
+      o3 = f4scale(f4add(f4add(a3[0], a3[1]), a3[2]), s3);
+      o5 = f4scale(f4add(f4add(f4add(a5[0], a5[1]), f4add(a5[2], a5[3])), a5[4]), s5);
+    }
+    if (x >= 0 && normalize) {
+      float sq[3] = {want1 ? f4dot(o1) : 0.f, want3 ? f4dot(o3) : 0.f, want5 ? f4dot(o5) : 0.f};
+      if (!active) sq[0] = sq[1] = sq[2] = 0.f;
+      block_sum<3>(sq, red, x & 1);  // its __syncthreads also frees this column's slot
+      o1 = f4scale(o1, 1.f / sqrtf(sq[0]));
+      o3 = f4scale(o3, 1.f / sqrtf(sq[1]));
+      o5 = f4scale(o5, 1.f / sqrtf(sq[2]));
+    } else {
+      __syncthreads();
+    }
+    if (threadIdx.x == 0 && xp + kBulkDepth < side && !aborted) {
+      tc::fence_proxy_async_smem();
+      issue(xp + kBulkDepth);
+    }
+    if (x >= 0 && active) {
+      const long long off = (long long)(y * side + x) * out_patch_stride;
+      if (want1) *reinterpret_cast<float4*>(o1p + off) = o1;
+      if (want3) *reinterpret_cast<float4*>(o3p + off) = o3;
+      if (want5) *reinterpret_cast<float4*>(o5p + off) = o5;
+    }
+  }
+  if (threadIdx.x == 0 && aborted) {
+    // Let copies still in flight land before the CTA's shared memory goes away.
+    const uint64_t start = global_ns();
+    for (int xc = side - kBulkDepth < 0 ? 0 : side - kBulkDepth; xc < side; ++xc) {
+      const uint32_t bar = tc::smem_u32(&full[xc % kBulkDepth]);
+      while (!tc::mbar_try_wait(bar, (uint32_t)(xc / kBulkDepth) & 1u) && global_ns() - start < kBulkWaitNs) {
+      }
     }
   }
 }
@@ -311,6 +453,36 @@ int stats_dispatch(const void* tokens, int dtype, int n_images, int tokens_per_i
 
 int block_threads(int channels) { return ((channels / 4 + 31) / 32) * 32; }
 
+// The staged stencil is the default; MUSC_B200_LNAMD_BULK=0 selects the
+// register-pipelined kernel (same outputs, bit for bit).
+int bulk_stencil_mode() {
+  const char* e = std::getenv("MUSC_B200_LNAMD_BULK");
+  return (e && e[0] == '0') ? 0 : 1;
+}
+
+template <typename T, int D, int NT, int MB>
+int launch_bulk(const void* tokens, int tokens_per_image, int channels, int side, const double* partial,
+                float* const* o, long long out_image_stride, long long out_patch_stride, int l2_normalize, int* err,
+                dim3 grid, int threads, cudaStream_t s) {
+  static std::mutex m;
+  static size_t done[64] = {0};
+  const size_t ring = (size_t)D * 5 * channels * sizeof(T);
+  int dev = 0;
+  MUSC_CUDA(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lock(m);
+    if (dev >= 64 || done[dev] < ring) {
+      MUSC_CUDA(cudaFuncSetAttribute(lnamd_stencil_bulk_kernel<T, D, NT, MB>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring));
+      if (dev < 64) done[dev] = ring;
+    }
+  }
+  lnamd_stencil_bulk_kernel<T, D, NT, MB><<<grid, threads, ring, s>>>(
+      static_cast<const T*>(tokens), tokens_per_image, channels, side, partial, o[0], o[1], o[2], out_image_stride,
+      out_patch_stride, l2_normalize, err);
+  return check_launch("lnamd_stencil_bulk_kernel");
+}
+
 }  // namespace
 }  // namespace musc
 
@@ -352,6 +524,41 @@ extern "C" int musc_b200_lnamd(const void* tokens, int dtype, int n_images, int 
   MUSC_TRY(stats_dispatch(tokens, dtype, n_images, tokens_per_image, channels, side, partial, s));
   dim3 grid(side, n_images);
   const int threads = block_threads(channels);
+  const int elem = dtype == MUSC_B200_F32 ? 4 : 2;
+  const int bulk = bulk_stencil_mode();
+  if ((channels * elem) % 16 == 0 && bulk != 0) {
+    int* err = device_error_ptr();
+    if (!err) return fail(MUSC_B200_ERR_CUDA, "lnamd: device error word unavailable");
+    // Up to 1024 channels: 256 threads, 2-deep ring, 3 CTAs per SM; wider rows: 512 threads, 3-deep.
+    if (threads <= 256) {
+      switch (dtype) {
+        case MUSC_B200_F32:
+          return launch_bulk<float, 2, 256, 3>(tokens, tokens_per_image, channels, side, partial, o, out_image_stride,
+                                               out_patch_stride, l2_normalize, err, grid, threads, s);
+        case MUSC_B200_F16:
+          return launch_bulk<__half, 2, 256, 3>(tokens, tokens_per_image, channels, side, partial, o, out_image_stride,
+                                                out_patch_stride, l2_normalize, err, grid, threads, s);
+        default:
+          return launch_bulk<__nv_bfloat16, 2, 256, 3>(tokens, tokens_per_image, channels, side, partial, o,
+                                                       out_image_stride, out_patch_stride, l2_normalize, err, grid,
+                                                       threads, s);
+      }
+    }
+    switch (dtype) {
+      case MUSC_B200_F32:
+        return launch_bulk<float, 3, kMaxStencilThreads, 1>(tokens, tokens_per_image, channels, side, partial, o,
+                                                            out_image_stride, out_patch_stride, l2_normalize, err,
+                                                            grid, threads, s);
+      case MUSC_B200_F16:
+        return launch_bulk<__half, 3, kMaxStencilThreads, 1>(tokens, tokens_per_image, channels, side, partial, o,
+                                                             out_image_stride, out_patch_stride, l2_normalize, err,
+                                                             grid, threads, s);
+      default:
+        return launch_bulk<__nv_bfloat16, 3, kMaxStencilThreads, 1>(tokens, tokens_per_image, channels, side, partial,
+                                                                    o, out_image_stride, out_patch_stride,
+                                                                    l2_normalize, err, grid, threads, s);
+    }
+  }
   switch (dtype) {
     case MUSC_B200_F32:
       lnamd_stencil_kernel<float><<<grid, threads, 0, s>>>(

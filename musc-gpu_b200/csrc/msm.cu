@@ -12,7 +12,9 @@
 //      is 128 query rows x 256 reference rows; per 32-wide K slice TMA brings
 //      A_hi, A_lo, B_hi, B_lo (48 KB) into a 4-deep shared-memory ring, and one
 //      thread issues hi*hi + hi*lo + lo*hi (6 MMAs of 128x256x16) into a
-//      fp32 TMEM accumulator (2 x 256 columns, double-buffered).  Four
+//      fp32 TMEM accumulator (2 x 256 columns, double-buffered).  The pool
+//      form runs as CTA pairs by default: 256 x 256 tiles, cta_group::2 MMAs of
+//      256x256x16, each CTA loading half of A and half of B.  Four
 //      epilogue warps read the accumulator (tcgen05.ld), form
 //      d^2 = |q|^2 + |r|^2 - 2 q.r, keep a running minimum per reference
 //      image segment and atomically lower nearest_sq[image][row].  The

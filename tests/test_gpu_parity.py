@@ -176,6 +176,28 @@ def _lib_device_error_clear() -> bool:
     return _lib.take_device_error() == _lib.OK
 
 
+@pytest.mark.parametrize('b,side,c,dtype,normalize,radii', [
+    (3, 7, 64, torch.float32, True, (1, 3, 5)), (2, 37, 1024, torch.float32, True, (1, 3, 5)),
+    (2, 37, 1024, torch.float16, False, (3,)), (2, 16, 256, torch.bfloat16, True, (5, 1)),
+    (2, 2, 32, torch.float32, True, (1, 3, 5)), (2, 9, 1028, torch.float16, True, (1, 3, 5))])
+def test_lnamd_staged_stencil_equals_register_stencil(cuda_device, monkeypatch, b, side, c, dtype, normalize,
+                                                      radii):
+    """The bulk-copy staged LNAMD stencil and the register-pipelined one give identical
+    outputs: every dtype, with and without the L2 normalisation, side 2 (fewer columns than
+    the copy ring), and a channel count whose fp16 rows are not 16-byte multiples (which
+    takes the register kernel either way)."""
+    from musc_b200 import ops
+    g = torch.Generator().manual_seed(side * 31 + c)
+    tokens = (torch.randn(b, 1 + side * side, c, generator=g) * 2 + 0.5).to(dtype).to(cuda_device)
+    res = {}
+    for bulk in ('0', '1'):
+        monkeypatch.setenv('MUSC_B200_LNAMD_BULK', bulk)
+        res[bulk] = ops.lnamd(tokens, radii, l2_normalize=normalize)
+    for a, bb in zip(res['0'], res['1']):
+        assert torch.equal(a, bb)
+    assert _lib_device_error_clear()
+
+
 def test_trimmed_mean_ties_and_offsets(cuda_device):
     from musc_b200 import ops
     gen = torch.Generator().manual_seed(5)
