@@ -211,6 +211,18 @@ int musc_b200_score_maps(const double* scores, int n_radii, int n_layers, int n,
                          int image_size, double* maps, double* image_max, double* upsampled,
                          musc_b200_stream stream);
 
+/* RsCIN image-score refinement (models/modules/_RsCIN.py:5-31, applied by
+ * models/musc.py:287-296).  cls_tokens [n_images][dim] float32 (the
+ * L2-normalised pooled class features), image_scores [n_images] float64 ->
+ * scores_out [n_images] float64 (must not alias image_scores).  For each k of
+ * k_list (at most 8 values, each <= min(n_images, 64)), every image averages
+ * the min-max normalised scores of the k images most similar to it (itself
+ * included) weighted by the similarity; the result is the mean over the
+ * list.  As in the reference, cls_tokens == NULL, n_k == 0 or a 0 in k_list
+ * returns the scores unchanged (a device copy). */
+int musc_b200_rscin(const float* cls_tokens, int n_images, int dim, const double* image_scores, int n_k,
+                    const int* k_list, double* scores_out, musc_b200_stream stream);
+
 /* ------------------------------------------------------------------------
  * Whole-pool scoring on one GPU (LNAMD, MSM and reduction in one call): the scoring
  * half of MuSc.make_category_data (models/musc.py:224-288) for non-Python

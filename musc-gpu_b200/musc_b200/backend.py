@@ -19,12 +19,13 @@ from __future__ import annotations
 import math
 from copy import deepcopy
 
+import numpy as np
 import torch
 
 from . import ops
 
 BACKENDS = ('original', 'gpu', 'super_fast', 'b200', 'b200_super_fast')
-_STATS = {'aggregation_calls': 0, 'direct_pool_calls': 0, 'msm_calls': 0}
+_STATS = {'aggregation_calls': 0, 'direct_pool_calls': 0, 'msm_calls': 0, 'rscin_calls': 0}
 
 
 def select_backend(requested: str, device_type: str, platform=None, device=None):
@@ -80,6 +81,29 @@ def MSM(Z: torch.Tensor, device=None, topmin_min: float = 0, topmin_max: float =
     """
     _STATS['msm_calls'] += 1
     return ops.msm(Z, topmin_min, topmin_max)
+
+
+# --------------------------------------------------------------------------- RsCIN
+def RsCIN(scores_old, cls_tokens=None, k_list=(0,), device=None):
+    """Drop-in for ``RsCIN`` (``models/modules/_RsCIN.py:22-31``) on the GPU.
+
+    Same arguments and passthrough rule: with ``cls_tokens`` None or a 0 in
+    ``k_list`` the scores come back unchanged (the same object).  Host inputs
+    (the numpy ``ac_score`` and list of class-token arrays that
+    ``models/musc.py:287-296`` passes) give a host float32 array, like the
+    reference; a CUDA float64 tensor gives a CUDA float64 tensor.
+    """
+    if cls_tokens is None or 0 in k_list:
+        return scores_old
+    _STATS['rscin_calls'] += 1
+    if isinstance(scores_old, torch.Tensor) and scores_old.is_cuda:
+        tokens = cls_tokens if isinstance(cls_tokens, torch.Tensor) else torch.as_tensor(
+            np.asarray(cls_tokens, dtype=np.float32))
+        return ops.rscin(scores_old.to(torch.float64), tokens.to(scores_old.device), k_list)
+    dev = torch.device(device) if device is not None else torch.device('cuda', torch.cuda.current_device())
+    scores = torch.as_tensor(np.asarray(scores_old, dtype=np.float64)).to(dev)
+    tokens = torch.as_tensor(np.asarray(cls_tokens, dtype=np.float32)).to(dev)
+    return ops.rscin(scores, tokens, k_list).cpu().numpy().astype(np.float32)
 
 
 # --------------------------------------------------------------------------- aggregation

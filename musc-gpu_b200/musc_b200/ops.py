@@ -286,6 +286,36 @@ def score_maps(scores: torch.Tensor, image_size: int = 518, upsampled: bool = Fa
     return maps, image_max, up
 
 
+def rscin(image_scores: torch.Tensor, cls_tokens: torch.Tensor | None,
+          k_list: Sequence[int] = (1, 2, 3)) -> torch.Tensor:
+    """RsCIN refinement of the per-image scores -> a new ``(N,)`` float64 tensor.
+
+    ``models/modules/_RsCIN.py:5-31``: the min-max normalised scores averaged over
+    each image's k most similar images (class-token similarity ``T T^T``, k in
+    ``k_list``), then the mean over ``k_list``; ``cls_tokens`` None or a 0 in
+    ``k_list`` return a copy of the scores, as in the reference.
+    """
+    _require_cuda(image_scores, 'rscin')
+    if image_scores.ndim != 1 or image_scores.dtype != torch.float64:
+        raise ValueError('rscin: expected (N,) float64 image scores')
+    n = image_scores.shape[0]
+    dev = image_scores.device
+    scores = image_scores.contiguous()
+    if cls_tokens is not None:
+        _require_cuda(cls_tokens, 'rscin')
+        if cls_tokens.ndim != 2 or cls_tokens.shape[0] != n or cls_tokens.device != dev:
+            raise ValueError('rscin: expected (N, dim) class tokens on the scores\' device')
+        cls_tokens = cls_tokens.to(torch.float32).contiguous()
+    ks = [int(k) for k in k_list]
+    arr = (ctypes.c_int * max(len(ks), 1))(*ks)
+    out = torch.empty(n, dtype=torch.float64, device=dev)
+    dim = cls_tokens.shape[1] if cls_tokens is not None else 0
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_rscin(_ptr(cls_tokens), n, dim, _ptr(scores), len(ks), arr, _ptr(out), _stream(dev))
+        _lib.check(st, 'musc_b200_rscin')
+    return out
+
+
 # --------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:

@@ -9,7 +9,9 @@ path the B200 library accelerates:
                           the interval average);
 * ``oracle.reduce``    -- layer/radius means, bilinear up-sampling and the
                           per-image maximum;
-* ``oracle.attention`` -- softmax attention of one multi-head block.
+* ``oracle.attention`` -- softmax attention of one multi-head block;
+* ``oracle.rscin``     -- the RsCIN image-score refinement from class-token
+                          similarities.
 
 Every function cites the reference file:line it follows.  Parity is pinned by
 ``tests/test_oracle_golden.py``, which checks these functions against golden

@@ -9,7 +9,8 @@ The script imports the reference's ``original`` modules --
 ``models/modules/_MSM.py`` (``MSM``), ``models/modules/_LNAMD.py``
 (``LNAMD._embed``), ``models/modules/_encoder_gpu.py``
 (``aggregate_features``), ``models/modules/_super_fast.py``
-(``SuperFastAggregation``) and the CLIP ``VisionTransformer``
+(``SuperFastAggregation``), ``models/modules/_RsCIN.py`` (``RsCIN``) and
+the CLIP ``VisionTransformer``
 (``models/backbone/open_clip/transformer.py``) -- and evaluates the score
 reduction of ``models/musc.py:259-288`` with the same torch calls.  Inputs are
 either stored in the fixture (small cases) or regenerated with the recorded
@@ -135,6 +136,26 @@ def make_pool16(MSM, LNAMD, encoder_gpu) -> dict:
             'bank_probe': bank_probe}
 
 
+def make_rscin_small(reference: str) -> dict:
+    """RsCIN (``models/modules/_RsCIN.py``) on stored class tokens and image scores, for the
+    k lists MuSc uses (``models/musc.py:290-295``: [1, 2, 3] for MVTec and the default,
+    [1, 8, 9] for VisA), plus the passthrough cases (k = 0, no class tokens)."""
+    sys.path.insert(0, reference)
+    from models.modules._RsCIN import RsCIN  # noqa: E402
+    g = torch.Generator().manual_seed(4321)
+    out = {}
+    for name, n, dim in (('a', 24, 768), ('b', 60, 768), ('c', 9, 64)):
+        tok = _unit_rows(torch.randn(n, dim, generator=g)).numpy().astype(np.float32)
+        score = (torch.rand(n, generator=g, dtype=torch.float64) * 0.5 + 1.0).numpy()
+        out[f'{name}_tokens'] = tok
+        out[f'{name}_scores'] = score
+        for kname, ks in (('k123', [1, 2, 3]), ('k189', [1, 8, 9])):
+            out[f'{name}_{kname}'] = np.asarray(RsCIN(score, list(tok), k_list=ks))
+        out[f'{name}_k0'] = np.asarray(RsCIN(score, list(tok), k_list=[0]))
+        out[f'{name}_none'] = np.asarray(RsCIN(score, None, k_list=[1, 2, 3]))
+    return out
+
+
 def _reference_vit_class(reference: str):
     """The reference's ``VisionTransformer`` (``models/backbone/open_clip/transformer.py``),
     imported under a stub package so ``open_clip/__init__.py`` (tokenizer, ftfy) is skipped."""
@@ -200,7 +221,8 @@ def main() -> None:
             'lnamd_small': lambda: make_lnamd_small(LNAMD, encoder_gpu, super_fast),
             'reduce_small': make_reduce_small,
             'pool16': lambda: make_pool16(MSM, LNAMD, encoder_gpu),
-            'encoder_pool6': lambda: make_encoder_pool(MSM, LNAMD, args.reference)}
+            'encoder_pool6': lambda: make_encoder_pool(MSM, LNAMD, args.reference),
+            'rscin_small': lambda: make_rscin_small(args.reference)}
     for name, job in jobs.items():
         if args.only and name not in args.only.split(','):
             continue

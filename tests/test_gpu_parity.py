@@ -325,3 +325,24 @@ def test_c_abi_score_pool_matches_pipeline_and_reference(cuda_device):
     assert torch.equal(mx, res.image_max)
     np.testing.assert_allclose(maps.view(n, 37, 37).cpu().numpy(), g['maps'], rtol=RTOL, atol=0)
     np.testing.assert_allclose(mx.cpu().numpy(), g['image_max'], rtol=RTOL, atol=0)
+
+
+def test_rscin_matches_reference(cuda_device):
+    """RsCIN on the GPU (musc_b200_rscin) against the reference's own RsCIN: the MVTec and
+    VisA k lists, N = 9 / 24 / 60, 64- and 768-dimensional class tokens; passthroughs."""
+    from musc_b200 import backend, ops
+    g = golden('rscin_small')
+    for c in 'abc':
+        tok, s = g[f'{c}_tokens'], g[f'{c}_scores']
+        for name, ks in (('k123', [1, 2, 3]), ('k189', [1, 8, 9])):
+            got = ops.rscin(torch.from_numpy(s).to(cuda_device), torch.from_numpy(tok).to(cuda_device), ks)
+            np.testing.assert_allclose(got.cpu().numpy(), g[f'{c}_{name}'], rtol=2e-6, atol=0)
+            host = backend.RsCIN(s, list(tok), k_list=ks, device=cuda_device)     # the musc.py call form
+            assert host.dtype == np.float32
+            np.testing.assert_allclose(host, g[f'{c}_{name}'], rtol=2e-6, atol=0)
+        assert backend.RsCIN(s, list(tok), k_list=[0]) is s
+        same = ops.rscin(torch.from_numpy(s).to(cuda_device), None, [1, 2, 3]).cpu().numpy()
+        np.testing.assert_array_equal(same, g[f'{c}_none'])
+    with pytest.raises(ValueError):
+        ops.rscin(torch.zeros(5, dtype=torch.float64, device=cuda_device),
+                  torch.zeros(5, 8, device=cuda_device), [6])              # k > N

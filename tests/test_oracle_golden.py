@@ -83,3 +83,16 @@ def test_pool16_banks_and_one_bank_scores():
     maps, image_max = oreduce.image_scores(g['scores'], 518)
     np.testing.assert_allclose(maps, g['maps'], rtol=0, atol=1e-14)
     np.testing.assert_allclose(image_max, g['image_max'], rtol=0, atol=1e-14)
+
+
+def test_rscin_oracle_matches_reference():
+    """oracle.rscin against RsCIN run by the reference (models/modules/_RsCIN.py): the k lists
+    MuSc uses, the k = 0 and no-class-token passthroughs."""
+    from oracle import rscin as orscin
+    g = golden('rscin_small')
+    for c in 'abc':
+        tok, s = g[f'{c}_tokens'], g[f'{c}_scores']
+        for name, ks in (('k123', [1, 2, 3]), ('k189', [1, 8, 9])):
+            np.testing.assert_allclose(orscin.rscin(s, list(tok), ks), g[f'{c}_{name}'], rtol=1e-6, atol=0)
+        np.testing.assert_array_equal(orscin.rscin(s, list(tok), [0]), g[f'{c}_k0'])
+        np.testing.assert_array_equal(orscin.rscin(s, None, [1, 2, 3]), g[f'{c}_none'])
