@@ -299,22 +299,27 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
       const int valid = p.tokens - j * BKV - half * (BKV / 2);  // keys past the sequence end are masked
       if (__all_sync(0xffffffffu, ok)) {
         tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < BKV / 64; ++c) {
-          uint32_t raw[32];
-          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(S_COL + sb * BKV + half * (BKV / 2) + c * 32), raw);
+        {
+          // both 32-column loads in flight before one wait
+          uint32_t raw0[32], raw1[32];
+          static_assert(BKV / 2 == 64, "two 32-column TMEM loads per half tile");
+          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(S_COL + sb * BKV + half * (BKV / 2)), raw0);
+          tc::tmem_ld_32x32b_x32(lane_base + (uint32_t)(S_COL + sb * BKV + half * (BKV / 2) + 32), raw1);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 32; ++t) sv[c * 32 + t] = __uint_as_float(raw[t]);
+          for (int t = 0; t < 32; ++t) sv[t] = __uint_as_float(raw0[t]), sv[32 + t] = __uint_as_float(raw1[t]);
         }
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(tc::smem_u32(&sm.s_empty[sb]));
+        // row maximum over four independent partial maxima (exact: max is order-free)
+        float mq[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
 #pragma unroll
         for (int c = 0; c < BKV / 2; ++c) {
           sv[c] = c < valid ? sv[c] * p.scale_log2 : -FLT_MAX;
-          mt = fmaxf(mt, sv[c]);
+          mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
         }
+        mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         sm.red[j & 1][half][r] = mt;
       } else {
         ok = false;
@@ -323,7 +328,7 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
       mt = fmaxf(mt, sm.red[j & 1][half ^ 1][r]);
       const float m_new = fmaxf(m_run, mt);
       const float alpha = ex2(m_run - m_new);
-      float lsum = 0.f;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial row sums
       uint8_t* prow = sm.p[sb] + half * (BQ * 128) + r * 128;  // this half's 64-key column block
 #pragma unroll
       for (int ch = 0; ch < BKV / 16; ++ch) {  // 16-byte chunks of 8 keys
@@ -332,12 +337,13 @@ attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
         for (int t = 0; t < 8; ++t) {
           const int c = ch * 8 + t;
           e[t] = c < valid ? ex2(sv[c] - m_new) : 0.f;
-          lsum += e[t];
+          ls[t & 3] += e[t];
         }
         uint4 pk = make_uint4(pack2<FP16>(e[0], e[1]), pack2<FP16>(e[2], e[3]), pack2<FP16>(e[4], e[5]),
                               pack2<FP16>(e[6], e[7]));
         *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
       }
+      const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
       l_half = l_half * alpha + lsum;
       m_run = m_new;
       tc::fence_proxy_async_smem();  // P stores -> visible to the tensor core
