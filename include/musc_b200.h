@@ -175,8 +175,11 @@ int musc_b200_nearest(const void* query_bank, long long query_rows, long long qu
  * scheduler uses; CTAs claim tiles from it, so ones that start late take
  * fewer.  max_ctas (0 = one per SM) caps the persistent grid: a multi-GPU
  * caller leaves a few SMs free so the collectives of the neighbouring banks
- * (which cannot share an SM with this kernel's 197 KB of shared memory) run
- * concurrently instead of after it.
+ * (which cannot share an SM with this kernel's ~200 KB of shared memory) run
+ * concurrently instead of after it.  The kernel runs as CTA pairs on two SMs
+ * (cta_group::2, 256 x 256 tiles; MUSC_B200_NEAREST_PAIR=0 in the
+ * environment selects single-CTA 128 x 256 tiles, same table bit for bit), so
+ * the cap is rounded down to an even number of CTAs.
  * rows_per_block = rows gives the plain [image][row] table;
  * rows_per_block = one rank's rows makes each rank's rows contiguous for a
  * reduce-scatter. */
