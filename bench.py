@@ -15,15 +15,16 @@ average) and the score reduction (maps, up-sampled image maxima).
   pipelined: step k+1's inputs are copied while step k computes).
 * ``roofline`` -- the dominant kernel (nearest_kernel) timed live with CUDA
   events on its stream: algorithmic flops 2*C*P^2*N*(N-1) per launch.
-* ``cpu_baseline`` -- the numpy oracle of the reference's ``original`` path on
-  the host cores, on a bounded sample, scaled to images/s.
+* ``cpu_baseline`` -- the reference's ``original`` path (restated with the same torch
+  CPU operations, ``oracle.torch_cpu``) on the host cores, on a bounded sample, scaled
+  to images/s.
 
 ``--gpus N`` under torchrun: rank r scores query images [r*ceil(N/G), ...)
 against the whole pool: banks are all-gathered over NCCL, each rank evaluates a
 balanced share of the symmetric distance tiles and a MIN reduce-scatter hands
 each rank its query rows' minima; the time is the max over ranks and ``value``
 counts the whole pool (strong scaling).
-``--impl reference`` times the CPU oracle port of the reference path instead.
+``--impl reference`` times that CPU port of the reference path instead.
 """
 from __future__ import annotations
 
@@ -141,45 +142,46 @@ class ClockSampler:
                 'samples': len(sm)}
 
 
-# ----------------------------------------------------------------- CPU oracle
+# ----------------------------------------------------------------- CPU baseline
 class CpuSample:
-    """Time the oracle (the reference's original path restated in numpy) on a bounded sample.
+    """Time the reference's original CPU path on a bounded sample.
 
-    Sample: LNAMD (r = 1, 3, 5) of 2 images of one layer, and the MSM rows of
-    one query image against the pool for one (layer, radius) bank.  Scaled to
-    a pool image: 4 layers of LNAMD + 12 banks of MSM rows.  Setup (the
-    pool's tokens and its r=3 bank) is untimed.
+    The timed code is ``oracle.torch_cpu``: the reference's ``LNAMD._embed`` and
+    ``compute_scores_fast`` restated with the same torch CPU operations (pinned bit for bit
+    to the reference's golden outputs), run with every host thread.  Sample: LNAMD
+    (r = 1, 3, 5, L2-normalised) of 2 images of one layer, and the MSM rows of one query
+    image against the pool for one (layer, radius) bank.  Scaled to a pool image: 4 layers
+    of LNAMD + 12 banks of MSM rows.  Setup (the pool's tokens and its r=3 bank) is untimed.
     """
 
     def __init__(self, pool: int, seed: int = 1):
         import torch
         from musc_b200.synthetic import prototype_mixture_layer
-        from oracle import lnamd as olnamd
-        from oracle import msm as omsm
+        from oracle import torch_cpu
         torch.set_num_threads(os.cpu_count() or 1)
-        self.olnamd, self.omsm = olnamd, omsm
-        self.tokens = prototype_mixture_layer(pool, generator=torch.Generator().manual_seed(seed)).numpy()
-        self.z = olnamd.bank(self.tokens, 3)
-        self.a, self.b = omsm.trimmed_ranks(pool)
+        self.torch_cpu = torch_cpu
+        self.tokens = prototype_mixture_layer(pool, generator=torch.Generator().manual_seed(seed))
+        self.z = torch_cpu.lnamd_bank(self.tokens, 3)
+        self.k_min, self.k_max = torch_cpu.interval(pool)
 
     def per_image_seconds(self) -> float:
         t0 = time.perf_counter()
         for r in RADII:
-            self.olnamd.bank(self.tokens[:2], r)
+            self.torch_cpu.lnamd_bank(self.tokens[:2], r)
         t_lnamd = (time.perf_counter() - t0) / 2          # per image, 3 radii, one layer
         t0 = time.perf_counter()
-        self.omsm.interval_average(self.omsm.nearest_minima(self.z, 0), self.a, self.b)
+        self.torch_cpu.msm_rows(self.z, 0, self.k_min, self.k_max)
         t_msm = time.perf_counter() - t0                  # one query image, one bank
         return N_LAYERS * t_lnamd + N_LAYERS * len(RADII) * t_msm
 
 
-CPU_SAMPLE_TEXT = ('numpy oracle of the reference original path: LNAMD r{1,3,5} of 2 images x 1 layer + '
-                   'MSM rows of 1 query image x 1 bank vs the whole pool, scaled to 4 layers x 12 banks '
-                   'per pool image')
+CPU_SAMPLE_TEXT = ('the reference original path (LNAMD._embed + compute_scores_fast) restated with the same '
+                   'torch CPU operations: LNAMD r{1,3,5} of 2 images x 1 layer + MSM rows of 1 query image x '
+                   '1 bank vs the whole pool, scaled to 4 layers x 12 banks per pool image')
 
 
 def run_reference(args):
-    """``--impl reference``: the oracle port of the reference's CPU path, rank 0 only."""
+    """``--impl reference``: the reference's CPU path (torch-CPU port, ``oracle.torch_cpu``), rank 0 only."""
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return

@@ -11,13 +11,16 @@ path the B200 library accelerates:
                           per-image maximum;
 * ``oracle.attention`` -- softmax attention of one multi-head block;
 * ``oracle.rscin``     -- the RsCIN image-score refinement from class-token
-                          similarities.
+                          similarities;
+* ``oracle.torch_cpu`` -- the timed CPU baseline: the reference's LNAMD and MSM
+                          with the same torch CPU operations (so its speed is the
+                          reference's; pinned bit for bit to the golden outputs).
 
 Every function cites the reference file:line it follows.  Parity is pinned by
 ``tests/test_oracle_golden.py``, which checks these functions against golden
 vectors produced by running the reference itself (``tests/golden``).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
-leg may import this package, and only as the checker or the timed CPU
+leg (and its ``--impl reference`` arm) may import this package, and only as the checker or the timed CPU
 baseline.  The product library never routes through it.
 """

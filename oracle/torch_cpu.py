@@ -1,0 +1,68 @@
+"""Timed CPU baseline: the reference's ``original`` path restated with the same torch
+CPU operations -- TEST / BENCHMARK INFRASTRUCTURE ONLY.
+
+``bench.py``'s CPU-baseline leg and ``--impl reference`` time this module on the host
+cores.  The numpy oracle (``oracle.lnamd``, ``oracle.msm``) is the parity checker; this
+module exists so the *timed* baseline runs the library calls the reference itself runs
+(the numpy restatement is 2-2.5x slower than the reference on the same cores, which would
+understate it).  Its results are pinned against the same golden fixtures.
+
+* ``lnamd_bank`` -- ``LNAMD._embed`` for one layer (``models/modules/_LNAMD.py:72-129``):
+  CLS dropped, ``(B, C, side, side)`` view, LayerNorm over ``(C, side, side)`` with unit
+  weight and zero bias (``:78-85``), r x r patches by ``unfold`` with zero padding
+  (``PatchMaker.patchify``, ``:16-34``; r = 1 is the plain reshape of ``:93-94``), the
+  per-channel window mean by ``adaptive_avg_pool1d`` over the flattened ``(C, r, r)``
+  patch (``MeanMapper``, ``:58-61``), then the L2 normalisation of ``models/musc.py:238``.
+* ``msm_rows`` -- ``compute_scores_fast`` (``models/modules/_MSM.py:10-30``) for one
+  query image: ``cdist`` against every other image's patches, the per-image minimum, the
+  two ``topk`` passes of the interval ``[k_min, k_max)`` and the mean.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def lnamd_bank(tokens: torch.Tensor, r: int, l2_normalize: bool = True) -> torch.Tensor:
+    """``(B, 1+P, C)`` fp32 CPU tokens -> ``(B, P, C)`` LNAMD features of radius ``r``."""
+    b, length, c = tokens.shape
+    side = math.isqrt(length - 1)
+    grid = tokens[:, 1:, :].reshape(b, side, side, c).permute(0, 3, 1, 2)
+    shape = [c, side, side]
+    grid = F.layer_norm(grid, shape, torch.ones(shape), torch.zeros(shape), 1e-5)
+    if r == 1:
+        patches = grid.reshape(b, c, -1, 1, 1).permute(0, 2, 1, 3, 4)
+    else:
+        cols = F.unfold(grid, kernel_size=r, padding=(r - 1) // 2, stride=1)     # (B, C*r*r, P)
+        patches = cols.reshape(b, c, r, r, -1).permute(0, 4, 1, 2, 3)          # (B, P, C, r, r)
+    flat = patches.reshape(-1, 1, c * r * r)
+    z = F.adaptive_avg_pool1d(flat, c).squeeze(1).reshape(b, -1, c)
+    if l2_normalize:
+        z = z / z.norm(dim=-1, keepdim=True)
+    return z
+
+
+def interval(n_images: int, topmin_min: float = 0.0, topmin_max: float = 0.3) -> tuple[int, int]:
+    """``(k_min, k_max)`` over the ``n_images - 1`` other images (``_MSM.py:19-27``)."""
+    k_max = int((n_images - 1) * topmin_max) if topmin_max < 1 else int(topmin_max)
+    k_min = int((n_images - 1) * topmin_min) if topmin_min < 1 else int(topmin_min)
+    return (k_max, k_min) if k_max < k_min else (k_min, k_max)
+
+
+def msm_rows(z: torch.Tensor, i: int, k_min: int, k_max: int) -> torch.Tensor:
+    """Scores ``(P,)`` of query image ``i`` of the bank ``z`` ``(N, P, C)``."""
+    n, p, c = z.shape
+    others = torch.cat((z[:i], z[i + 1:]), dim=0).reshape(-1, c)
+    dist = torch.cdist(z[i:i + 1], others).reshape(p, n - 1, p)
+    nearest = dist.min(dim=-1).values                                             # (P, N-1)
+    low = torch.topk(nearest.float(), k_max, largest=False, sorted=True).values
+    band = torch.topk(low.float(), k_max - k_min, largest=True, sorted=True).values
+    return band.mean(dim=1)
+
+
+def msm(z: torch.Tensor, topmin_min: float = 0.0, topmin_max: float = 0.3) -> torch.Tensor:
+    """``(N, P, C)`` -> ``(N, P)`` float64 (``_MSM.py:53-59``)."""
+    k_min, k_max = interval(z.shape[0], topmin_min, topmin_max)
+    return torch.stack([msm_rows(z, i, k_min, k_max) for i in range(z.shape[0])]).double()

@@ -96,3 +96,21 @@ def test_rscin_oracle_matches_reference():
             np.testing.assert_allclose(orscin.rscin(s, list(tok), ks), g[f'{c}_{name}'], rtol=1e-6, atol=0)
         np.testing.assert_array_equal(orscin.rscin(s, list(tok), [0]), g[f'{c}_k0'])
         np.testing.assert_array_equal(orscin.rscin(s, None, [1, 2, 3]), g[f'{c}_none'])
+
+
+def test_timed_cpu_port_matches_reference_exactly():
+    """oracle.torch_cpu (the timed CPU baseline: the reference's original path with the same
+    torch CPU operations) reproduces the reference's LNAMD._embed and MSM outputs bit for bit."""
+    import torch
+    from oracle import torch_cpu
+    g = golden('lnamd_small')
+    tokens = torch.from_numpy(g['tokens'])                          # (layers, B, 1+P, C)
+    for r in (1, 3, 5):
+        for layer in range(tokens.shape[0]):
+            got = torch_cpu.lnamd_bank(tokens[layer], r, l2_normalize=False).numpy()
+            np.testing.assert_array_equal(got, g[f'embed_r{r}'][:, :, layer, :])
+    g = golden('msm_small')
+    for c in 'abcde':
+        lo, hi = (float(v) for v in g[f'{c}_ranks'])
+        got = torch_cpu.msm(torch.from_numpy(g[f'{c}_z']), lo, hi).numpy()
+        np.testing.assert_array_equal(got, g[f'{c}_scores'])
