@@ -1,0 +1,56 @@
+/* A C99 host of the musc_b200 C ABI: compiled with gcc -std=c99 against
+ * include/musc_b200.h and linked to the built library by tests/test_c_abi.py.
+ * It makes host-only calls (no device work): the ABI version, the size
+ * queries and contract violations that every entry point reports before any
+ * CUDA call, with their status codes and messages. */
+#include <stdio.h>
+#include <string.h>
+
+#include "musc_b200.h"
+
+static int failures = 0;
+
+static void expect(int cond, const char* what) {
+  if (!cond) {
+    fprintf(stderr, "FAIL: %s (last error: %s)\n", what, musc_b200_last_error());
+    ++failures;
+  }
+}
+
+int main(void) {
+  expect(musc_b200_abi_version() == 1, "abi version");
+  expect(musc_b200_lnamd_workspace_bytes(4) == 4 * 8 * 2 * sizeof(double), "lnamd workspace");
+  expect(musc_b200_bank_bytes(1369, 1024) % 1024 == 0, "bank bytes aligned");
+  expect(musc_b200_nearest_pool_bytes(16 * 1369, 1369, 16 * 1369) >= (size_t)16 * 16 * 1369 * 4,
+         "nearest table bytes");
+  expect(musc_b200_score_pool_bytes(16, 1370, 1024, 3) > musc_b200_bank_bytes(16 * 1369, 1024),
+         "score pool workspace");
+  expect(musc_b200_score_pool_bytes(0, 1370, 1024, 3) == 0, "score pool workspace, no images");
+
+  size_t planes[4];
+  expect(musc_b200_bank_layout(1369, 1024, planes) == MUSC_B200_OK, "bank layout");
+  expect(planes[0] == 0 && planes[1] > planes[0] && planes[2] > planes[1] && planes[3] > planes[2],
+         "bank planes ordered");
+
+  /* contract violations: reported before any CUDA call */
+  expect(musc_b200_trimmed_mean(NULL, 10, 5, 0, 1, NULL, NULL) == MUSC_B200_ERR_INVALID, "trimmed null");
+  expect(strstr(musc_b200_last_error(), "null") != NULL, "trimmed null message");
+  int radii[1] = {2};
+  float* outs[1] = {(float*)(size_t)1024};
+  expect(musc_b200_lnamd((const void*)(size_t)1024, MUSC_B200_F32, 2, 1370, 64, 1, radii, outs,
+                         1369 * 64, 64, 1, (void*)(size_t)1024, 1024, NULL) == MUSC_B200_ERR_INVALID,
+         "lnamd radius");
+  int ks[9] = {1, 2, 3, 4, 5, 6, 7, 8, 9};
+  expect(musc_b200_rscin((const float*)(size_t)1024, 10, 768, (const double*)(size_t)2048, 9, ks,
+                         (double*)(size_t)4096, NULL) == MUSC_B200_ERR_INVALID,
+         "rscin k list");
+  expect(musc_b200_msm((const float*)(size_t)16, 1, 10, 8, 0, 1, (double*)(size_t)16,
+                       (void*)(size_t)1024, (size_t)1 << 30, NULL) == MUSC_B200_ERR_INVALID,
+         "msm N>=2");
+  int code = -1;
+  expect(musc_b200_take_device_error(NULL) == MUSC_B200_ERR_INVALID, "device error null");
+  (void)code;
+
+  if (failures == 0) printf("c abi ok\n");
+  return failures == 0 ? 0 : 1;
+}
