@@ -17,7 +17,10 @@
 //      LayerNorm rstd and -- when asked -- divides by the per-patch L2 norm
 //      over channels (one block reduction per patch).  All radii come from one
 //      read of the tokens; the five input rows a CTA reads are re-read by the
-//      neighbouring rows' CTAs, which run next to it, mostly from L2.
+//      neighbouring rows' CTAs, which run next to it, mostly from L2.  The
+//      default (staged) form streams each column's input tokens into a
+//      shared-memory ring with bulk copies; the register-pipelined form
+//      serves rows whose byte length is not a multiple of 16.
 // Algorithmic bytes per layer: n * (1 + P) * C * sizeof(T) read for the
 // statistics, the same again for the stencil, and n_radii * n * P * C * 4
 // written.

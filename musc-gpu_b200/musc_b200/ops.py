@@ -208,7 +208,8 @@ def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, par
     with one part the single block is the full ``(n_images, rows)`` table.
     ``out`` must come from :func:`nearest_pool_table` (it carries the scheduler word).
     ``bank_rows``: the row count the bank is laid out for (a padded gathered bank).
-    ``max_ctas``: cap on the persistent grid (0 = one CTA per SM).
+    ``max_ctas``: cap on the persistent grid (0 = one CTA per SM; the default CTA-pair
+    kernel rounds it down to an even count).
     """
     dev = bank.device
     rpb = rows if rows_per_block is None else rows_per_block
