@@ -59,9 +59,9 @@ def _args():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--pool', type=int, default=None, help='pool size (default: the config\'s)')
-    ap.add_argument('--config', default='2', choices=['2', '3', '4', '5'],
-                    help='BASELINE.json config: 2 (default, the metric\'s), 3 super-fast, 4 N=1024, '
-                         '5 encoder end to end')
+    ap.add_argument('--config', default='2', choices=['1', '2', '3', '4', '5'],
+                    help='BASELINE.json config: 1 (N=16, the reference arm runs it in full), 2 (default, '
+                         'the metric\'s), 3 super-fast, 4 N=1024, 5 encoder end to end')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--collective-sms', type=int, default=0,
                     help='SMs left free for NCCL during each bank GEMM (multi-GPU; 0 = none)')
@@ -144,66 +144,105 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- CPU baseline
 class CpuSample:
-    """Time the reference's original CPU path on a bounded sample.
+    """Time the reference's original CPU path on the host cores.
 
-    The timed code is ``oracle.torch_cpu``: the reference's ``LNAMD._embed`` and
-    ``compute_scores_fast`` restated with the same torch CPU operations (pinned bit for bit
-    to the reference's golden outputs), run with every host thread.  Sample: LNAMD
-    (r = 1, 3, 5, L2-normalised) of 2 images of one layer, and the MSM rows of one query
-    image against the pool for one (layer, radius) bank.  Scaled to a pool image: 4 layers
-    of LNAMD + 12 banks of MSM rows.  Setup (the pool's tokens and its r=3 bank) is untimed.
+    The timed code is ``oracle.torch_cpu``: the reference's ``LNAMD._embed``,
+    ``SuperFastAggregation`` and ``compute_scores_fast`` restated with the same torch CPU
+    operations (pinned bit for bit to the reference's golden outputs), with every host
+    thread.  ``full`` runs the whole pool (LNAMD of every layer and radius, MSM of every
+    bank) -- config 1 (N = 16), about a minute.  Otherwise one call is a bounded sample:
+    LNAMD of 2 images of one layer (all radii) and the MSM rows of one query image against
+    the whole pool for one bank, extrapolated to a pool image (layers x LNAMD + banks x MSM
+    rows).  Setup (the pool's tokens and one bank) is untimed.
     """
 
-    def __init__(self, pool: int, seed: int = 1):
+    def __init__(self, cfg: dict, pool: int, full: bool, seed: int = 1):
         import torch
-        from musc_b200.synthetic import prototype_mixture_layer
+        from musc_b200.synthetic import prototype_mixture, prototype_mixture_layer
         from oracle import torch_cpu
         torch.set_num_threads(os.cpu_count() or 1)
         self.torch_cpu = torch_cpu
-        self.tokens = prototype_mixture_layer(pool, generator=torch.Generator().manual_seed(seed))
-        self.z = torch_cpu.lnamd_bank(self.tokens, 3)
+        self.cfg, self.pool, self.full = cfg, pool, full
+        self.layers, self.radii, self.sf = cfg['layers'], cfg['radii'], cfg['super_fast']
+        if full:
+            self.tokens = prototype_mixture(pool, n_layers=self.layers, seed=seed)
+        else:
+            self.tokens = [prototype_mixture_layer(pool, generator=torch.Generator().manual_seed(seed))]
+            self.z = self._bank(self.tokens[0], self.radii[-1])
         self.k_min, self.k_max = torch_cpu.interval(pool)
 
-    def per_image_seconds(self) -> float:
-        t0 = time.perf_counter()
-        for r in RADII:
-            self.torch_cpu.lnamd_bank(self.tokens[:2], r)
-        t_lnamd = (time.perf_counter() - t0) / 2          # per image, 3 radii, one layer
+    def _bank(self, tokens, r):
+        if self.sf:
+            return self.torch_cpu.lnamd_super_fast(tokens, self.sf)
+        return self.torch_cpu.lnamd_bank(tokens, r)
+
+    def run(self) -> tuple[float, float]:
+        """One step: ``(wall seconds, seconds per pool image)``."""
+        t_start = time.perf_counter()
+        if self.full:
+            for layer in self.tokens:
+                for r in self.radii:
+                    self.torch_cpu.msm(self._bank(layer, r), 0.0, 0.3)
+            wall = time.perf_counter() - t_start
+            return wall, wall / self.pool
+        for r in self.radii:
+            self._bank(self.tokens[0][:2], r)
+        t_lnamd = (time.perf_counter() - t_start) / 2          # per image, all radii, one layer
         t0 = time.perf_counter()
         self.torch_cpu.msm_rows(self.z, 0, self.k_min, self.k_max)
-        t_msm = time.perf_counter() - t0                  # one query image, one bank
-        return N_LAYERS * t_lnamd + N_LAYERS * len(RADII) * t_msm
+        t_msm = time.perf_counter() - t0                       # one query image, one bank
+        wall = time.perf_counter() - t_start
+        return wall, self.layers * t_lnamd + self.layers * len(self.radii) * t_msm
+
+    def describe(self) -> str:
+        what = ('LNAMD._embed + compute_scores_fast' if not self.sf else
+                'SuperFastAggregation (r=3 LNAMD + adaptive_avg_pool2d) + compute_scores_fast')
+        head = f'the reference original path ({what}) restated with the same torch CPU operations'
+        if self.full:
+            return f'{head}: the whole pool (N={self.pool}, {self.layers} layers x {len(self.radii)} radii) per step'
+        tail = (f'; one step = LNAMD of 2 images x 1 layer (all radii) + MSM rows of 1 query image x 1 bank vs '
+                f'the whole pool (N={self.pool}), extrapolated to {self.layers} layers x '
+                f'{self.layers * len(self.radii)} banks per pool image')
+        if self.cfg.get('encoder'):
+            tail += '; the ViT encoder\'s CPU time is not included (favours the reference)'
+        return head + tail
 
 
-CPU_SAMPLE_TEXT = ('the reference original path (LNAMD._embed + compute_scores_fast) restated with the same '
-                   'torch CPU operations: LNAMD r{1,3,5} of 2 images x 1 layer + MSM rows of 1 query image x '
-                   '1 bank vs the whole pool, scaled to 4 layers x 12 banks per pool image')
+def cpu_measure(cfg: dict, pool: int, full: bool, steps: int, warmup: int) -> dict:
+    """Run ``warmup`` + ``steps`` CPU steps; the numbers of the timed ones."""
+    sample = CpuSample(cfg, pool, full)
+    for _ in range(max(warmup, 0)):
+        sample.run()
+    runs = [sample.run() for _ in range(max(steps, 1))]
+    walls, per_image = zip(*runs)
+    return {'value': 1.0 / statistics.median(per_image), 'ms_per_step': statistics.median(walls) * 1e3,
+            'wall_s': sum(walls), 'cores': os.cpu_count() or 1, 'sample': sample.describe(),
+            'extrapolated': not full}
 
 
 def run_reference(args):
-    """``--impl reference``: the reference's CPU path (torch-CPU port, ``oracle.torch_cpu``), rank 0 only."""
+    """``--impl reference``: the reference's CPU path (torch-CPU port, ``oracle.torch_cpu``), rank 0 only.
+
+    Every reported step ran: ``ms_per_step`` is the median wall time of one step (the whole
+    pool for config 1, one bounded sample otherwise, marked ``extrapolated``), so
+    ``steps * ms_per_step`` is the timed region's length.
+    """
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
     sys.path.insert(0, str(REPO))
-    cores = os.cpu_count() or 1
-    pool = args.pool if args.pool is not None else N_POOL
-    sample = CpuSample(pool)
-    for _ in range(max(args.warmup, 0)):
-        sample.per_image_seconds()
-    times = [sample.per_image_seconds() for _ in range(args.steps)]
-    per_image = statistics.median(times)
-    value = 1.0 / per_image
+    cfg = CONFIGS[args.config]
+    pool = args.pool if args.pool is not None else cfg['pool']
+    m = cpu_measure(cfg, pool, args.config == '1', args.steps, args.warmup)
     line = {
-        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
-        'warmup': args.warmup, 'ms_per_step': per_image * pool * 1e3, 'higher_is_better': True,
+        'metric': METRIC, 'value': m['value'], 'unit': UNIT, 'n_gpus': args.gpus, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': m['ms_per_step'], 'higher_is_better': True,
         'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'impl': 'reference',
-        'config': {'workload': f'config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32',
-                   'global_batch': pool, 'l2': 'inputs larger than L2'},
-        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                         'sample': CPU_SAMPLE_TEXT},
-        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'impl': 'reference', 'extrapolated': m['extrapolated'],
+        'config': config_of(args, cfg, pool, 1 if args.gpus < 1 else args.gpus),
+        'cpu_baseline': {'value': m['value'], 'unit': UNIT, 'cores': m['cores'], 'kind': 'port',
+                         'sample': m['sample'], 'extrapolated': m['extrapolated']},
+        'e2e': {'value': m['value'], 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -223,6 +262,9 @@ def symmetric_tiles(rows: int, patches: int, n_images: int, bm: int = 128, bn: i
 
 # ----------------------------------------------------------------- GPU arm
 CONFIGS = {
+    '1': dict(pool=16, layers=4, radii=(1, 3, 5), super_fast=None, encoder=False,
+              desc='config1: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 prototype-mixture '
+                   'tokens resident in HBM'),
     '2': dict(pool=100, layers=4, radii=(1, 3, 5), super_fast=None, encoder=False,
               desc='config2: pool N={pool}, 4 layers x r{{1,3,5}}, P=1369, C=1024 fp32 prototype-mixture '
                    'tokens resident in HBM'),
@@ -236,6 +278,16 @@ CONFIGS = {
                    'fused attention) on N={pool} seeded 518x518x3 U[0,1] images, batch 4, hooks 6/12/18/24, '
                    'then LNAMD r{{1,3,5}} + MSM + reduction'),
 }
+
+
+def config_of(args, cfg: dict, pool: int, world: int) -> dict:
+    """The line's ``config``: the same dict for both arms of one command."""
+    p_score = cfg['super_fast'] ** 2 if cfg['super_fast'] else P
+    tok_bytes = cfg['layers'] * pool * (P + 1) * C * 4
+    return {'workload': cfg['desc'].format(pool=pool), 'global_batch': pool, 'seq_len': p_score,
+            'parallelism': f'query-shard{world}',
+            'l2': (f'inputs larger than L2 ({tok_bytes / 1e9:.2f} GB of tokens per step); no flush'
+                   if not cfg['encoder'] else 'encoder activations and banks larger than L2; no flush')}
 
 
 def run_b200(args):
@@ -446,6 +498,19 @@ def run_b200(args):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
     ops.attention = orig_attention
+    # Every bounded device-side wait completed in the timed runs (else: RuntimeError, no line).
+    ops.check_device_error(dev, 'bench')
+
+    # ---- sharded parity (N > 1): every rank re-scores the last bank of one more pool step
+    # as one whole-pool part from the gathered bank and compares its own query rows with
+    # the sharded scores bit for bit (untimed).
+    parity = None
+    if group is not None:
+        res = pipeline.score_pool(tokens_of(resident), n_images=pool, radii=radii, group=group, kernels=ops,
+                                  super_fast_side=sf, verify=True)
+        parity = res.verified
+        torch.cuda.synchronize()
+        ops.check_device_error(dev, 'bench parity')
 
     stats = torch.tensor([elapsed_ms, e2e_ms, sum(near_ms) / max(len(near_ms), 1)], dtype=torch.float64,
                          device=dev)
@@ -472,9 +537,7 @@ def run_b200(args):
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
             'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-            'config': {'workload': cfg['desc'].format(pool=pool), 'global_batch': pool, 'seq_len': p_score,
-                       'parallelism': f'query-shard{world}',
-                       'l2': f'inputs larger than L2 ({h2d * world / 1e9:.2f} GB per step); no flush'},
+            'config': config_of(args, cfg, pool, world),
             'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
                     'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
             'roofline': {'kernel': 'nearest_kernel', 'bound': 'tensor', 'achieved': achieved_tflops,
@@ -498,13 +561,16 @@ def run_b200(args):
                                      'frac': at / peaks.get('bf16_tflops'), 'launches': len(attn_events),
                                      'ms_per_pool': attn_ms, 'timed_on': 'one eager encoder pass',
                                      'peak_kind': f'{peak_kind} bf16 burst (short launches)'}
-        if not args.no_cpu_baseline and args.config == '2':
+        if parity is not None:
+            line['parity'] = parity
+        if not args.no_cpu_baseline and world == 1 and args.config != '1':
+            # rank 0 at N = 1 only (no other rank is waiting meanwhile); the same sampler as
+            # the reference arm, so the two CPU figures agree on the same host
             sys.path.insert(0, str(REPO))
-            sample = CpuSample(pool)
-            sample.per_image_seconds()
-            per_image = statistics.median(sample.per_image_seconds() for _ in range(3))
-            line['cpu_baseline'] = {'value': 1.0 / per_image, 'unit': UNIT, 'cores': os.cpu_count(),
-                                    'kind': 'port', 'sample': CPU_SAMPLE_TEXT}
+            m = cpu_measure(cfg, pool, False, 3, 1)
+            line['cpu_baseline'] = {'value': m['value'], 'unit': UNIT, 'cores': m['cores'], 'kind': 'port',
+                                    'sample': m['sample'], 'extrapolated': m['extrapolated'],
+                                    'timed_s': round(m['wall_s'], 2)}
         print(json.dumps(line), flush=True)
     if group is not None:
         dist.barrier(device_ids=[local_rank])

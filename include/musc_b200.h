@@ -53,7 +53,16 @@ int musc_b200_abi_version(void);
 const char* musc_b200_last_error(void);
 
 /* Reads and clears the device-side error word of the current device
- * (MUSC_B200_OK or MUSC_B200_ERR_TIMEOUT).  Synchronises the device. */
+ * (MUSC_B200_OK or MUSC_B200_ERR_TIMEOUT).  Synchronises the device.
+ *
+ * The pipelined kernels (nearest GEMM, attention, staged LNAMD stencil) never
+ * hang: a bounded wait that expires sets this word and the kernel returns
+ * early, leaving its output incomplete.  While the word is set, the interval
+ * average (musc_b200_trimmed_mean, musc_b200_msm, musc_b200_score_pool), the
+ * score maps and RsCIN write NaN instead of scores, so an incomplete result is
+ * never a plausible number.  Callers of musc_b200_score_pool, musc_b200_msm,
+ * musc_b200_nearest_pool, musc_b200_nearest and musc_b200_attention_fwd call
+ * this once, where they synchronise anyway, before trusting the outputs. */
 int musc_b200_take_device_error(int* code);
 
 /* Self-test of the device-side bounded wait that every pipelined kernel here
@@ -99,9 +108,10 @@ int musc_b200_lnamd(const void* tokens, int dtype, int n_images, int tokens_per_
  * array in the library's static device memory, so:
  *   - at most 2048 images per call; larger n_images returns
  *     MUSC_B200_ERR_INVALID before any work is enqueued;
- *   - the first call on a device looks the array's address up for that
- *     device (cudaGetSymbolAddress) -- make that first call before any stream
- *     capture on the device;
+ *   - every call looks the array's address up for the current device
+ *     (cudaGetSymbolAddress, a host-side query that allocates nothing; the
+ *     first one on a device may load the library's module there) -- make the
+ *     first call on a device before any stream capture on it;
  *   - every call shares the one array: nothing in it needs to start at zero
  *     (each call overwrites the slots it reads before reading them), but calls
  *     that overlap on the GPU -- concurrent streams, or other host threads --
@@ -191,12 +201,16 @@ int musc_b200_nearest_pool(const void* bank, long long bank_rows, long long rows
 
 /* Interval average: scores[q] = mean of ranks [rank_lo, rank_hi) of
  * sqrt(nearest_sq[:, q]) over the n_images - 1 other images, in float32,
- * stored as float64 (_MSM.py:19-30).  0 <= rank_lo < rank_hi <= n_images-1. */
+ * stored as float64 (_MSM.py:19-30).  0 <= rank_lo < rank_hi <= n_images-1.
+ * Pool size limit: a CTA stages 32 rows x n_images keys in shared memory, so
+ * n_images <= 1790 on a B200 (227 KB per CTA); larger pools return
+ * MUSC_B200_ERR_INVALID (the reference's MSM has no such limit). */
 int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
                            int rank_lo, int rank_hi, double* scores, musc_b200_stream stream);
 
 /* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64.
- * The workspace holds the bank and the nearest table. */
+ * The workspace holds the bank and the nearest table.  n <= 1790 (the
+ * interval average's shared-memory limit, see musc_b200_trimmed_mean). */
 size_t musc_b200_msm_workspace_bytes(int n, int p, int c);
 
 int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi,

@@ -225,7 +225,9 @@ lnamd_stencil_bulk_kernel(const T* __restrict__ tokens, int tokens_per_image, in
   const int y_hi = y + 2 > side - 1 ? side - 1 : y + 2;
   const uint32_t col_bytes = (uint32_t)(y_hi - y_lo + 1) * row_bytes;
 
+  __shared__ int last_issued;  // thread 0: the last column whose copies were issued
   auto issue = [&](int xc) {  // thread 0: column xc into slot xc % kBulkDepth
+    last_issued = xc;
     const int slot = xc % kBulkDepth;
     const uint32_t bar = tc::smem_u32(&full[slot]);
     tc::mbar_arrive_expect_tx(bar, col_bytes);
@@ -237,6 +239,7 @@ lnamd_stencil_bulk_kernel(const T* __restrict__ tokens, int tokens_per_image, in
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBulkDepth; ++s) tc::mbar_init(tc::smem_u32(&full[s]), 1);
     aborted = 0;
+    last_issued = -1;
     tc::fence_barrier_init();
     for (int xc = 0; xc < kBulkDepth && xc < side; ++xc) issue(xc);
   }
@@ -320,9 +323,14 @@ lnamd_stencil_bulk_kernel(const T* __restrict__ tokens, int tokens_per_image, in
     }
   }
   if (threadIdx.x == 0 && aborted) {
-    // Let copies still in flight land before the CTA's shared memory goes away.
+    // Let copies still in flight land before the CTA's shared memory goes away.  Only
+    // the last kBulkDepth issued columns can be in flight: each occupies its own slot,
+    // armed for that column's phase and never re-armed, so waiting on that phase's
+    // parity waits for exactly those copies (earlier columns of the same slots were
+    // consumed before the slot was reused; columns never issued are not waited on).
     const uint64_t start = global_ns();
-    for (int xc = side - kBulkDepth < 0 ? 0 : side - kBulkDepth; xc < side; ++xc) {
+    const int first = last_issued - kBulkDepth + 1 < 0 ? 0 : last_issued - kBulkDepth + 1;
+    for (int xc = first; xc <= last_issued; ++xc) {
       const uint32_t bar = tc::smem_u32(&full[xc % kBulkDepth]);
       while (!tc::mbar_try_wait(bar, (uint32_t)(xc / kBulkDepth) & 1u) && global_ns() - start < kBulkWaitNs) {
       }
@@ -642,22 +650,15 @@ __device__ __align__(256) double g_lnamd_noalloc_scratch[kNoAllocMaxImages * kSt
 
 // Device address of the scratch array on the current device.  Host code may
 // not pass the array's name to a kernel (on the host it is only a stand-in
-// symbol), so the address is looked up once per device with that device
-// current and cached.
+// symbol), so the address is looked up with the device current.  It is looked
+// up on every call (a host-side query that allocates nothing) rather than
+// cached, so a context torn down and recreated (cudaDeviceReset) never leaves
+// a stale address behind.
 int noalloc_scratch(double** out) {
-  static std::mutex m;
-  static std::vector<double*> ptrs;
-  int dev = 0;
-  MUSC_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(m);
-  if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    cudaError_t err = cudaGetSymbolAddress(&p, g_lnamd_noalloc_scratch);
-    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(g_lnamd_noalloc_scratch)");
-    ptrs[dev] = static_cast<double*>(p);
-  }
-  *out = ptrs[dev];
+  void* p = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&p, g_lnamd_noalloc_scratch);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(g_lnamd_noalloc_scratch)");
+  *out = static_cast<double*>(p);
   return MUSC_B200_OK;
 }
 

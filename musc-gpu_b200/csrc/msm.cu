@@ -722,8 +722,11 @@ struct SelRow {
 
 __global__ void __launch_bounds__(kSelThreads)
 trimmed_mean_kernel(const unsigned int* __restrict__ nearest, long long q_rows, int n, int pitch,
-                    int rank_lo, int rank_hi, double* __restrict__ scores) {
+                    int rank_lo, int rank_hi, double* __restrict__ scores, const int* err) {
   extern __shared__ unsigned int tile[];  // [kSelRows][pitch]
+  // A bounded wait that expired earlier on this device (device error word set and not yet
+  // taken) means some table may be incomplete: every score becomes NaN instead.
+  const bool poisoned = *reinterpret_cast<const volatile int*>(err) != 0;
   const long long row0 = (long long)blockIdx.x * kSelRows;
   for (int idx = threadIdx.x; idx < n * kSelRows; idx += kSelThreads) {
     const int j = idx / kSelRows, r = idx - j * kSelRows;
@@ -750,7 +753,8 @@ trimmed_mean_kernel(const unsigned int* __restrict__ nearest, long long q_rows, 
   }
   const double hi = sel.sum_smallest(rank_hi, kmin, kmax);
   const double lo = sel.sum_smallest(rank_lo, kmin, kmax);
-  if (sub == 0) scores[row] = (double)(float)((hi - lo) / (double)(rank_hi - rank_lo));
+  if (sub == 0) scores[row] = poisoned ? __longlong_as_double(0x7FF8000000000000LL)
+                                      : (double)(float)((hi - lo) / (double)(rank_hi - rank_lo));
 }
 
 // ------------------------------------------------------------------ host helpers
@@ -999,9 +1003,12 @@ int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, 
   if ((long long)smem > smem_optin() - 1024)
     return fail(MUSC_B200_ERR_INVALID, "trimmed_mean: too many images for shared memory (N <= ~1700)");
   MUSC_CUDA(cudaFuncSetAttribute(trimmed_mean_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int* err = device_error_ptr();
+  if (!err) return fail(MUSC_B200_ERR_CUDA, "trimmed_mean: device error word unavailable");
   const long long blocks = (query_rows + kSelRows - 1) / kSelRows;
   trimmed_mean_kernel<<<(unsigned)blocks, kSelThreads, smem, s>>>(
-      reinterpret_cast<const unsigned int*>(nearest_sq), query_rows, n_images, pitch, rank_lo, rank_hi, scores);
+      reinterpret_cast<const unsigned int*>(nearest_sq), query_rows, n_images, pitch, rank_lo, rank_hi, scores,
+      err);
   return check_launch("trimmed_mean_kernel");
 }
 

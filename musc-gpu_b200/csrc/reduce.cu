@@ -26,10 +26,13 @@ constexpr int kReduceThreads = 256;
 __global__ void __launch_bounds__(kReduceThreads)
 score_maps_kernel(const double* __restrict__ scores, int n_radii, int n_layers, int n, int side,
                   int image_size, double* __restrict__ maps, double* __restrict__ image_max,
-                  double* __restrict__ upsampled) {
+                  double* __restrict__ upsampled, const int* err) {
   extern __shared__ double map[];
   const int img = blockIdx.x;
   const int P = side * side;
+  // Device error word set (an expired bounded wait upstream): NaN maps and maxima.
+  const double nan = __longlong_as_double(0x7FF8000000000000LL);
+  const bool poisoned = *reinterpret_cast<const volatile int*>(err) != 0;
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     double acc_r = 0.0;
     for (int r = 0; r < n_radii; ++r) {
@@ -38,7 +41,7 @@ score_maps_kernel(const double* __restrict__ scores, int n_radii, int n_layers, 
         acc_l += scores[(((long long)r * n_layers + l) * n + img) * P + p];
       acc_r += acc_l / (double)n_layers;
     }
-    const double v = acc_r / (double)n_radii;
+    const double v = poisoned ? nan : acc_r / (double)n_radii;
     map[p] = v;
     maps[(long long)img * P + p] = v;
   }
@@ -70,7 +73,7 @@ score_maps_kernel(const double* __restrict__ scores, int n_radii, int n_layers, 
   if (threadIdx.x == 0) {
     double b = red[0];
     for (int w = 1; w < kReduceThreads / 32; ++w) b = red[w] > b ? red[w] : b;
-    image_max[img] = b;
+    image_max[img] = poisoned ? nan : b;
   }
 }
 
@@ -85,7 +88,7 @@ struct KList {
 
 __global__ void __launch_bounds__(kRscinThreads)
 rscin_kernel(const float* __restrict__ cls, int n, int dim, const double* __restrict__ scores, KList klist,
-             int kmax, double* __restrict__ out) {
+             int kmax, double* __restrict__ out, const int* err) {
   extern __shared__ float w[];  // row i of W
   __shared__ double red_lo[kRscinThreads / 32], red_hi[kRscinThreads / 32];
   __shared__ float red_v[kRscinThreads / 32];
@@ -167,7 +170,9 @@ rscin_kernel(const float* __restrict__ cls, int n, int dim, const double* __rest
       }
       acc += num / den;
     }
-    out[i] = acc / (double)klist.count;
+    // Device error word set (an expired bounded wait upstream): NaN instead of a score.
+    out[i] = *reinterpret_cast<const volatile int*>(err) != 0 ? __longlong_as_double(0x7FF8000000000000LL)
+                                                              : acc / (double)klist.count;
   }
 }
 
@@ -208,7 +213,10 @@ extern "C" int musc_b200_rscin(const float* cls_tokens, int n_images, int dim, c
     return fail(MUSC_B200_ERR_INVALID, "rscin: too many images for one similarity row in shared memory");
   if (smem > 48 * 1024)
     MUSC_CUDA(cudaFuncSetAttribute(rscin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  rscin_kernel<<<n_images, kRscinThreads, smem, s>>>(cls_tokens, n_images, dim, image_scores, kl, kmax, scores_out);
+  int* err = device_error_ptr();
+  if (!err) return fail(MUSC_B200_ERR_CUDA, "rscin: device error word unavailable");
+  rscin_kernel<<<n_images, kRscinThreads, smem, s>>>(cls_tokens, n_images, dim, image_scores, kl, kmax, scores_out,
+                                                     err);
   return check_launch("rscin_kernel");
 }
 
@@ -221,7 +229,9 @@ extern "C" int musc_b200_score_maps(const double* scores, int n_radii, int n_lay
   const size_t smem = (size_t)side * side * sizeof(double);
   if (smem > 48 * 1024) return fail(MUSC_B200_ERR_INVALID, "score_maps: side too large (side*side <= 6144)");
   MUSC_TRY(require_sm100());
+  int* err = device_error_ptr();
+  if (!err) return fail(MUSC_B200_ERR_CUDA, "score_maps: device error word unavailable");
   score_maps_kernel<<<n, kReduceThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      scores, n_radii, n_layers, n, side, image_size, maps, image_max, upsampled);
+      scores, n_radii, n_layers, n, side, image_size, maps, image_max, upsampled, err);
   return check_launch("score_maps_kernel");
 }

@@ -68,19 +68,12 @@ int smem_optin(void) {
   return d.smem_optin;
 }
 
+// Looked up on every call (a host-side query) instead of cached, so a context
+// that was torn down and recreated never leaves a stale address behind.
 int* device_error_ptr(void) {
-  static std::mutex m;
-  static std::vector<int*> ptrs;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  std::lock_guard<std::mutex> lock(m);
-  if ((int)ptrs.size() <= dev) ptrs.resize(dev + 1, nullptr);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, musc_device_error) != cudaSuccess) return nullptr;
-    ptrs[dev] = static_cast<int*>(p);
-  }
-  return ptrs[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, musc_device_error) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
 }
 
 }  // namespace musc

@@ -77,7 +77,11 @@ def configure_backend(cfg: dict, device_type: str, platform=None) -> dict:
 def MSM(Z: torch.Tensor, device=None, topmin_min: float = 0, topmin_max: float = 0.3) -> torch.Tensor:
     """``scoring`` seam: ``(N, P, C)`` CUDA fp32 -> ``(N, P)`` float64 on ``Z.device``.
 
-    Same contract and errors as ``models/modules/_MSM_gpu.py:701-711``.
+    Same contract and errors as ``models/modules/_MSM_gpu.py:701-711``, with one
+    limit the reference does not have: ``N <= 1790`` (the interval average stages
+    32 rows x N minima in shared memory); larger pools raise ``ValueError``.
+    Asynchronous like the reference: if a device-side bounded wait expired, the
+    scores are NaN; :func:`musc_b200.ops.check_device_error` reports it.
     """
     _STATS['msm_calls'] += 1
     return ops.msm(Z, topmin_min, topmin_max)
@@ -103,7 +107,9 @@ def RsCIN(scores_old, cls_tokens=None, k_list=(0,), device=None):
     dev = torch.device(device) if device is not None else torch.device('cuda', torch.cuda.current_device())
     scores = torch.as_tensor(np.asarray(scores_old, dtype=np.float64)).to(dev)
     tokens = torch.as_tensor(np.asarray(cls_tokens, dtype=np.float32)).to(dev)
-    return ops.rscin(scores, tokens, k_list).cpu().numpy().astype(np.float32)
+    host = ops.rscin(scores, tokens, k_list).cpu().numpy().astype(np.float32)
+    ops.check_device_error(dev, 'RsCIN')      # the copy above synchronised already
+    return host
 
 
 # --------------------------------------------------------------------------- aggregation
@@ -134,7 +140,11 @@ def aggregate_features(layer, features, return_cpu: bool = True) -> torch.Tensor
     _STATS['aggregation_calls'] += 1
     if layer.r != 1:
         _STATS['direct_pool_calls'] += 1
-    return result.cpu() if return_cpu else result
+    if not return_cpu:
+        return result
+    host = result.cpu()
+    ops.check_device_error(result.device, 'aggregation')   # the copy above synchronised already
+    return host
 
 
 class Aggregation:
@@ -164,7 +174,11 @@ class SuperFastAggregation(Aggregation):
         if side != 37 or len(tokens) != 1 or layer.r != 3:
             raise ValueError('super_fast requires one layer, r=3 and a37x37 source patch grid')
         out = ops.lnamd_super_fast(first, self.PATCH_GRID, l2_normalize=False).unsqueeze(2)
-        return out.cpu() if return_cpu else out
+        if not return_cpu:
+            return out
+        host = out.cpu()
+        ops.check_device_error(out.device, 'aggregation')
+        return host
 
 
 def new_aggregation() -> Aggregation:

@@ -39,6 +39,23 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
         raise ValueError(f'{what}: expected a CUDA tensor (the b200 backend has no CPU path)')
 
 
+def check_device_error(device=None, what: str = 'musc_b200') -> None:
+    """Raise ``RuntimeError`` if a bounded device-side wait expired since the last check.
+
+    The pipelined kernels never hang: a wait that runs out sets the device's
+    error word and the kernel returns early, and from then on the selection,
+    map and RsCIN kernels write NaN instead of scores until the word is taken.
+    This reads and clears the word (it synchronises the device), so callers
+    use it where they synchronise anyway -- after copying results to the host.
+    """
+    dev = torch.device(device) if device is not None else torch.device('cuda', torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        code = _lib.take_device_error()
+    if code != _lib.OK:
+        raise RuntimeError(f'{what}: a device-side bounded wait expired (status {code}); '
+                           'the outputs since the last check are NaN or incomplete')
+
+
 # --------------------------------------------------------------------------- LNAMD
 def lnamd(tokens: torch.Tensor, radii: Sequence[int] = (1, 3, 5), l2_normalize: bool = True,
           out: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:

@@ -50,13 +50,14 @@ class PoolScores:
     image_max: torch.Tensor   # (n_local,) float64
     first_image: int
     n_images: int
+    verified: dict | None = None   # sharded-vs-whole check of the last bank (``verify=True``)
 
 
 def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
                radii: Sequence[int] = (1, 3, 5), topmin_min: float = 0, topmin_max: float = 0.3,
                image_size: int = 518, super_fast_side: int | None = None,
                group=None, kernels=ops, ready: Sequence | None = None,
-               collective_sms: int = 16) -> PoolScores:
+               collective_sms: int = 0, verify: bool = False) -> PoolScores:
     """Score one pool from device-resident tokens.
 
     ``tokens``: per hooked layer, this rank's ``(n_local, 1+P, C)`` tokens
@@ -70,7 +71,13 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     l's event just before that layer's LNAMD, so later layers' copies overlap
     the scoring of earlier ones.  Banks are processed layer by layer.
     ``collective_sms``: with a process group, SMs left free during each bank's
-    GEMM so the neighbouring banks' gather and reduce-scatter run alongside it.
+    GEMM so the neighbouring banks' gather and reduce-scatter run alongside it
+    (0 = none, the default: the GEMM's dynamic tile scheduler already lets a
+    collective that starts first keep its SMs).
+    ``verify``: with a process group, re-score the last bank on every rank as one
+    whole-pool part from the gathered bank and compare the rows each rank owns
+    with the sharded result, bit for bit; the outcome (summed over ranks) is in
+    ``PoolScores.verified``.  Off the timed path: it costs one more bank.
     """
     import torch.distributed as dist
 
@@ -125,6 +132,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     #    whose blocks are the ranks' query rows; a MIN reduce-scatter (overlapping the
     #    next bank's GEMM) hands each rank the minima of its own rows.
     banks = [(li, ri) for li in range(n_l) for ri in range(n_r)]
+    verified = None
     scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
     rows = n_images * p
     q_rows = n_local * p
@@ -185,6 +193,10 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         for finish, kk in pending:
             finish()
             select(mine[kk % 3], *banks[kk])
+        if verify:
+            verified = _verify_last_bank(kernels, full_bank[(len(banks) - 1) % 2], bank_rows, rows, c, p,
+                                         n_images, first, q_rows, a, b, scores[banks[-1][1], banks[-1][0]],
+                                         banks[-1], group)
 
     # 3. Layer/radius means, up-sampling, image maxima for the local images.
     if n_local:
@@ -192,7 +204,30 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     else:
         maps = torch.empty(0, side, side, dtype=torch.float64, device=dev)
         image_max = torch.empty(0, dtype=torch.float64, device=dev)
-    return PoolScores(scores, maps, image_max, first, n_images)
+    return PoolScores(scores, maps, image_max, first, n_images, verified)
+
+
+def _verify_last_bank(kernels, bank, bank_rows, rows, c, p, n_images, first, q_rows, a, b, got, bank_id, group):
+    """Every rank scores the gathered bank as one part (the single-GPU computation) and
+    compares its own query rows with the sharded scores ``got``; counts summed over ranks."""
+    import torch.distributed as dist
+    dev = got.device
+    whole = kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, bank_rows=bank_rows)[0]   # (N, rows)
+    mism = torch.zeros(3, dtype=torch.float64, device=dev)
+    if q_rows:
+        mine = whole[:, first * p:first * p + q_rows].contiguous()
+        ref = kernels.trimmed_mean(mine, a, b)
+        sharded = got.reshape(-1)
+        diff = (ref - sharded).abs()
+        mism[0] = (ref != sharded).sum()
+        mism[1] = diff.max()
+        mism[2] = q_rows
+    dist.all_reduce(mism[0:1], group=group)
+    dist.all_reduce(mism[1:2], op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(mism[2:3], group=group)
+    bad, worst, checked = mism.tolist()
+    return {'bank': {'layer': bank_id[0], 'radius_index': bank_id[1]}, 'rows_checked': int(checked),
+            'rows_differing': int(bad), 'max_abs_diff': worst, 'bit_exact': bad == 0}
 
 
 _SIDE_GROUPS: dict = {}

@@ -33,17 +33,27 @@ def trimmed_ranks(n_images: int, topmin_min: float = 0, topmin_max: float = 0.3)
     return int(k_min), int(k_max)
 
 
-def nearest_minima(Z: np.ndarray, i: int) -> np.ndarray:
-    """``(P, N-1)`` float32 minima of query image ``i`` (``_MSM.py:14-17``)."""
+def nearest_minima(Z: np.ndarray, i: int, chunk: int | None = None) -> np.ndarray:
+    """``(P, N-1)`` float32 minima of query image ``i`` (``_MSM.py:14-17``).
+
+    ``chunk``: evaluate the reference images in groups of this many (same arithmetic per
+    (query, reference) pair; bounds the ``P x chunk*P`` distance block for large pools).
+    """
     Z = np.asarray(Z, dtype=np.float32)
     n, p, c = Z.shape
     q = Z[i]
-    ref = np.concatenate([Z[:i], Z[i + 1:]], axis=0).reshape(-1, c)
+    others = [j for j in range(n) if j != i]
+    step = len(others) if chunk is None else max(1, int(chunk))
     qn = np.einsum('ij,ij->i', q, q, dtype=np.float32)
-    rn = np.einsum('ij,ij->i', ref, ref, dtype=np.float32)
-    d2 = qn[:, None] + rn[None, :] - np.float32(2) * (q @ ref.T)
-    d = np.sqrt(np.maximum(d2, np.float32(1e-30)))
-    return d.reshape(p, n - 1, p).min(axis=2)
+    out = []
+    for s in range(0, len(others), step):
+        ids = others[s:s + step]
+        ref = Z[ids].reshape(-1, c)
+        rn = np.einsum('ij,ij->i', ref, ref, dtype=np.float32)
+        d2 = qn[:, None] + rn[None, :] - np.float32(2) * (q @ ref.T)
+        d = np.sqrt(np.maximum(d2, np.float32(1e-30)))
+        out.append(d.reshape(p, len(ids), p).min(axis=2))
+    return np.concatenate(out, axis=1)
 
 
 def interval_average(minima: np.ndarray, k_min: int, k_max: int) -> np.ndarray:

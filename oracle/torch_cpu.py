@@ -44,6 +44,27 @@ def lnamd_bank(tokens: torch.Tensor, r: int, l2_normalize: bool = True) -> torch
     return z
 
 
+def lnamd_super_fast(tokens: torch.Tensor, out_side: int = 28, l2_normalize: bool = True) -> torch.Tensor:
+    """Super-fast profile on CPU: ``SuperFastAggregation.__call__`` (``models/modules/_super_fast.py:17-27``).
+
+    The r = 3 direct-pool LNAMD of ``aggregate_features`` (``models/modules/_encoder_gpu.py:14-42``:
+    ``layer_norm`` with unit weight and zero bias, ``avg_pool2d(3, 1, 1,
+    count_include_pad=True)``), then ``adaptive_avg_pool2d`` to ``out_side`` x ``out_side`` in
+    float32, then the L2 normalisation of ``models/musc.py:238``.  ``(B, 1+P, C)`` -> ``(B, out_side^2, C)``.
+    """
+    b, length, c = tokens.shape
+    side = math.isqrt(length - 1)
+    shape = (c, side, side)
+    spatial = tokens[:, 1:].reshape(b, side, side, c).permute(0, 3, 1, 2)
+    spatial = F.layer_norm(spatial, shape, torch.ones(shape), torch.zeros(shape))
+    spatial = F.avg_pool2d(spatial, 3, stride=1, padding=1, count_include_pad=True)
+    pooled = F.adaptive_avg_pool2d(spatial.float(), (out_side, out_side))
+    z = pooled.reshape(b, c, out_side * out_side).permute(0, 2, 1).contiguous()
+    if l2_normalize:
+        z = z / z.norm(dim=-1, keepdim=True)
+    return z
+
+
 def interval(n_images: int, topmin_min: float = 0.0, topmin_max: float = 0.3) -> tuple[int, int]:
     """``(k_min, k_max)`` over the ``n_images - 1`` other images (``_MSM.py:19-27``)."""
     k_max = int((n_images - 1) * topmin_max) if topmin_max < 1 else int(topmin_max)

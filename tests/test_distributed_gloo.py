@@ -62,9 +62,11 @@ class OracleKernels:
         return out
 
     @staticmethod
-    def nearest_pool(bank, rows, c, p, part, parts, rpb, out, bank_rows=None, max_ctas=0):
+    def nearest_pool(bank, rows, c, p, part, parts, rpb, out=None, bank_rows=None, max_ctas=0):
         """Squared minima for the image pairs {i, j} with min(i, j) % parts == part."""
         n = rows // p
+        if out is None:
+            out = torch.empty(-(-rows // rpb), n, rpb)
         z = bank[:rows].numpy().reshape(n, p, c).astype(np.float64)
         out.fill_(float(np.finfo(np.float32).max))
         for i in range(n):
@@ -78,7 +80,9 @@ class OracleKernels:
         return out
 
     @staticmethod
-    def trimmed_mean(near, a, b, out):
+    def trimmed_mean(near, a, b, out=None):
+        if out is None:
+            out = torch.empty(near.shape[1], dtype=torch.float64)
         d = np.sort(np.sqrt(near.numpy().astype(np.float64)), axis=0)[a:b]
         out.copy_(torch.from_numpy(d.mean(axis=0).astype(np.float32).astype(np.float64)))
         return out
@@ -108,10 +112,10 @@ def _rank_main(rank, world, port, queue):
         first, end, _ = shard_range(N_IMAGES, world, rank)
         local = [t[first:end].contiguous() for t in _tokens()]
         res = score_pool(local, n_images=N_IMAGES, radii=RADII, image_size=40, group=dist.group.WORLD,
-                         kernels=OracleKernels())
+                         kernels=OracleKernels(), verify=True)
         maps, mx = gather_pool(res, dist.group.WORLD)
         if rank == 0:
-            queue.put((maps.numpy(), mx.numpy(), res.scores.numpy()))
+            queue.put((maps.numpy(), mx.numpy(), res.scores.numpy(), res.verified))
     finally:
         dist.destroy_process_group()
 
@@ -125,7 +129,7 @@ def test_sharded_pool_equals_single_process(world):
     procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue)) for r in range(world)]
     for p in procs:
         p.start()
-    maps, mx, scores0 = queue.get(timeout=240)
+    maps, mx, scores0, verified = queue.get(timeout=240)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -133,3 +137,7 @@ def test_sharded_pool_equals_single_process(world):
     np.testing.assert_array_equal(mx, single.image_max.numpy())
     first, end, _ = shard_range(N_IMAGES, world, 0)
     np.testing.assert_array_equal(scores0, single.scores.numpy()[:, :, first:end])
+    # the in-run check the bench reports: every rank's rows of the last bank, re-scored as
+    # one whole-pool part, equal the sharded scores bit for bit
+    assert verified['bit_exact'] and verified['rows_differing'] == 0
+    assert verified['rows_checked'] == N_IMAGES * SIDE * SIDE

@@ -346,3 +346,46 @@ def test_rscin_matches_reference(cuda_device):
     with pytest.raises(ValueError):
         ops.rscin(torch.zeros(5, dtype=torch.float64, device=cuda_device),
                   torch.zeros(5, 8, device=cuda_device), [6])              # k > N
+
+
+def test_config4_pool_sampled_images_against_oracle(cuda_device):
+    """Config 4 size: N = 1024 images of 1369 patches (C = 64 to keep the oracle short).
+    LNAMD r = 3 on the GPU, then the MSM of the whole 1.4 M-row bank (symmetric tiles,
+    blocked table, interval over the 306 smallest of 1023 minima); the first, a middle and
+    the last query image against the oracle's minima and interval average."""
+    from musc_b200 import ops
+    from musc_b200.synthetic import prototype_mixture_layer
+    n, c = 1024, 64
+    tokens = prototype_mixture_layer(n, c=c, generator=torch.Generator().manual_seed(44))
+    z = ops.lnamd(tokens.to(cuda_device), (3,), l2_normalize=True)[0]
+    del tokens
+    scores = ops.msm(z).cpu().numpy()
+    zc = z.cpu().numpy()
+    del z
+    a, b = omsm.trimmed_ranks(n)
+    assert (a, b) == (0, 306)
+    for i in (0, 511, 1023):
+        want = omsm.interval_average(omsm.nearest_minima(zc, i, chunk=64), a, b)
+        np.testing.assert_allclose(scores[i], want, rtol=RTOL, atol=0)
+    assert _lib_device_error_clear()
+
+
+def test_config3_super_fast_pool100_against_oracle(cuda_device):
+    """Config 3 size: N = 100, one layer, r = 3 then 37x37 -> 28x28 (784 patches), C = 1024,
+    through score_pool's super-fast profile; sampled query images against the oracle's
+    super-fast banks, minima and interval average, and the image maxima of those images."""
+    from musc_b200.pipeline import score_pool
+    from musc_b200.synthetic import prototype_mixture_layer
+    n = 100
+    tokens = prototype_mixture_layer(n, generator=torch.Generator().manual_seed(33))
+    res = score_pool([tokens.to(cuda_device)], super_fast_side=28)
+    got = res.scores[0, 0].cpu().numpy()
+    mx = res.image_max.cpu().numpy()
+    z = olnamd.l2_normalize(olnamd.lnamd_super_fast(tokens.numpy(), 28))
+    a, b = omsm.trimmed_ranks(n)
+    for i in (0, 57, 99):
+        want = omsm.interval_average(omsm.nearest_minima(z, i), a, b)
+        np.testing.assert_allclose(got[i], want, rtol=RTOL, atol=0)
+        _, want_mx = oreduce.image_scores(want[None, None, None], 518)
+        np.testing.assert_allclose(mx[i], want_mx[0], rtol=RTOL, atol=0)
+    assert _lib_device_error_clear()

@@ -109,6 +109,9 @@ def test_timed_cpu_port_matches_reference_exactly():
         for layer in range(tokens.shape[0]):
             got = torch_cpu.lnamd_bank(tokens[layer], r, l2_normalize=False).numpy()
             np.testing.assert_array_equal(got, g[f'embed_r{r}'][:, :, layer, :])
+    # super-fast: SuperFastAggregation's r = 3 direct pool + adaptive pooling (unnormalised)
+    got = torch_cpu.lnamd_super_fast(tokens[0], 28, l2_normalize=False).numpy()
+    np.testing.assert_allclose(got, g['superfast'][:, :, 0, :], rtol=1e-5, atol=2e-6)
     g = golden('msm_small')
     for c in 'abcde':
         lo, hi = (float(v) for v in g[f'{c}_ranks'])

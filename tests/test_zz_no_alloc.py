@@ -49,6 +49,26 @@ def test_noalloc_lnamd_matches_workspace_entry_point(cuda_device):
             torch.testing.assert_close(g, w, rtol=1e-5, atol=2e-5)
 
 
+def test_noalloc_lnamd_fp16_and_the_image_limit(cuda_device):
+    """fp16 tokens, and one call at exactly the 2048-image limit (a 4 x 4 patch grid,
+    C = 64), so the last scratch slots are written and read; each against the
+    workspace entry point, twice in a row."""
+    from musc_b200 import ops
+    gen = torch.Generator().manual_seed(77)
+    radii = (1, 3, 5)
+    batches = [((torch.randn(4, 1370, 96, generator=gen) * 2.0 - 0.3).to(torch.float16), True),
+               (torch.randn(2048, 1 + 16, 64, generator=gen) * 1.5 + 0.2, True),
+               ((torch.randn(2048, 1 + 16, 64, generator=gen) + 1.0).to(torch.float16), False)]
+    for tokens, l2 in batches:
+        tokens = tokens.to(cuda_device)
+        want = ops.lnamd(tokens, radii, l2_normalize=l2)
+        got = [torch.full_like(w, float('nan')) for w in want]
+        _noalloc(tokens, radii, got, l2)
+        torch.cuda.synchronize()
+        for g, w in zip(got, want):
+            torch.testing.assert_close(g, w, rtol=1e-5, atol=2e-5)
+
+
 def test_noalloc_rejects_batches_beyond_the_scratch(cuda_device):
     from musc_b200 import _lib
     radii = (ctypes.c_int * 1)(3)
