@@ -75,12 +75,13 @@ def _peaks():
         return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
 
 
-def _traffic():
-    """DRAM bytes per nearest_kernel launch from the committed ncu summary (or None)."""
+def _traffic(exact_path: bool):
+    """DRAM bytes per launch of the dominant GEMM at config 2, from the committed ncu summary
+    (or None when no capture of that kernel variant is committed)."""
     f = REPO / 'profiles' / 'nearest_kernel_traffic.json'
     try:
         d = json.loads(f.read_text())
-        return d.get('bytes_per_launch_config2')
+        return d.get('bytes_per_launch_config2' if exact_path else 'screen_bytes_per_launch_config2')
     except Exception:
         return None
 
@@ -337,12 +338,17 @@ def run_b200(args):
 
     # ---- our kernels, instrumented: launch counts and the dominant kernel's event timing
     near_events, launches = [], [0]
-    per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'prep_bank': 1, 'nearest_pool': 2, 'trimmed_mean': 1,
-                'score_maps': 1}
+    # our kernels per call: lnamd = statistics + stencil; nearest_pool = fill + GEMM; screen_pool = GEMM
+    # (its fills are memsets); refine = image bounds, refinement, fallback plan, gather, gathered GEMM,
+    # rescue
+    per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'prep_bank': 1, 'nearest_pool': 2, 'screen_pool': 1,
+                'refine': 6, 'trimmed_mean': 1, 'score_maps': 1}
+    gemm_ops = ('nearest_pool', 'screen_pool')
 
     class Kernels:
         trimmed_ranks = staticmethod(ops.trimmed_ranks)
         nearest_pool_table = staticmethod(ops.nearest_pool_table)
+        screen_table = staticmethod(ops.screen_table)
         empty_bank = staticmethod(ops.empty_bank)
         bank_planes = staticmethod(ops.bank_planes)
     kern = Kernels()
@@ -359,7 +365,7 @@ def run_b200(args):
             e0.record(st)
             out = fn(*a, **k)
             e1.record(st)
-            (near_events if name == 'nearest_pool' else op_events.setdefault(name, [])).append((e0, e1))
+            (near_events if name in gemm_ops else op_events.setdefault(name, [])).append((e0, e1))
             return out
         return call
     for name in per_call:
@@ -427,7 +433,10 @@ def run_b200(args):
     elapsed_ms = t0.elapsed_time(t1)
     near_ms = [a.elapsed_time(b) for a, b in near_events]
     op_ms = {name: sum(a.elapsed_time(b) for a, b in evs) / args.steps for name, evs in op_events.items()}
-    op_ms['nearest_pool'] = sum(near_ms) / args.steps
+    from musc_b200.pipeline import exact_pool_path
+    exact_path = exact_pool_path()
+    op_ms['nearest_pool' if exact_path else 'screen_pool'] = sum(near_ms) / args.steps
+    refine_ms = [a.elapsed_time(b) for a, b in op_events.get('refine', [])]
     launches_timed = launches[0]
     # attention: timed on one eager encoder pass (the timed steps replay CUDA graphs);
     # 4 * L^2 * d flop per (batch item, head), head_dim 64
@@ -512,11 +521,11 @@ def run_b200(args):
         torch.cuda.synchronize()
         ops.check_device_error(dev, 'bench parity')
 
-    stats = torch.tensor([elapsed_ms, e2e_ms, sum(near_ms) / max(len(near_ms), 1)], dtype=torch.float64,
-                         device=dev)
+    stats = torch.tensor([elapsed_ms, e2e_ms, sum(near_ms) / max(len(near_ms), 1),
+                          sum(refine_ms) / max(len(refine_ms), 1)], dtype=torch.float64, device=dev)
     if group is not None:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, near_avg_ms = stats.tolist()
+    elapsed_ms, e2e_ms, near_avg_ms, refine_avg_ms = stats.tolist()
 
     if rank == 0:
         peaks, peak_kind = _peaks()
@@ -525,12 +534,16 @@ def run_b200(args):
         # algorithmic (directed) MSM flops per bank, 2*C*P^2*N*(N-1) (the count the reference's
         # original path computes); each rank's launch covers 1/world of the pool's tiles
         msm_flop_per_bank = 2.0 * C * p_score * p_score * pool * (pool - 1)
-        achieved_tflops = msm_flop_per_bank / world / (near_avg_ms / 1e3) / 1e12
-        # executed tensor-core work: 3 MMA passes over the symmetric tiles (whole tiles holding
-        # a pair of different images, each pair once; 256 x 256 for the CTA-pair kernel, 128 x 256
-        # for the single-CTA one), this rank's share
+        # the MSM contraction's time per bank: the GEMM plus (default path) the refinement to
+        # exact minima; effective rate = the directed algorithmic flops over that time
+        msm_ms = near_avg_ms + (0.0 if exact_path else refine_avg_ms)
+        achieved_tflops = msm_flop_per_bank / world / (msm_ms / 1e3) / 1e12
+        # executed tensor-core work of the GEMM alone: MMA passes (3 exact, 1 screened) over the
+        # symmetric tiles (whole tiles holding a pair of different images, each pair once; 256 x 256
+        # for the CTA-pair kernel, 128 x 256 for the single-CTA one), this rank's share
         tile_m = 256 if os.environ.get('MUSC_B200_NEAREST_PAIR', '1') != '0' else 128
-        mma_tflops = (3 * 2.0 * symmetric_tiles(pool * p_score, p_score, pool, bm=tile_m) * tile_m * 256 * C
+        passes = 3 if exact_path else 1
+        mma_tflops = (passes * 2.0 * symmetric_tiles(pool * p_score, p_score, pool, bm=tile_m) * tile_m * 256 * C
                       / world / (near_avg_ms / 1e3) / 1e12)
         peak = peaks.get('bf16_tflops_sustained', peaks.get('bf16_tflops'))
         line = {
@@ -540,14 +553,19 @@ def run_b200(args):
             'config': config_of(args, cfg, pool, world),
             'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
                     'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
-            'roofline': {'kernel': 'nearest_kernel', 'bound': 'tensor', 'achieved': achieved_tflops,
+            'roofline': {'kernel': ('nearest_kernel<symmetric>' if exact_path
+                                    else 'nearest_kernel<screen> + refinement'),
+                         'bound': 'tensor', 'achieved': achieved_tflops,
                          'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved_tflops / peak,
-                         'traffic': _traffic() if (args.config == '2' and pool == N_POOL) else None,
+                         'traffic': _traffic(exact_path) if (args.config == '2' and pool == N_POOL) else None,
                          'peak_kind': f'{peak_kind} bf16 sustained (kernel timed inside a long step)',
                          'mma_executed_tflops': mma_tflops, 'mma_frac': mma_tflops / peak,
-                         'mma_kind': ('kind::f16 cta_group::%d (fp16 split hi/lo, 3 passes, symmetric %dx256 tiles)'
-                                     % (2 if tile_m == 256 else 1, tile_m)),
-                         'launch_ms': near_avg_ms},
+                         'mma_kind': ('kind::f16 cta_group::%d (fp16 %s, symmetric %dx256 tiles)'
+                                      % (2 if tile_m == 256 else 1,
+                                         'split hi/lo, 3 passes' if exact_path else 'hi only, 1 screening pass',
+                                         tile_m)),
+                         'gemm_ms_per_bank': near_avg_ms, 'refine_ms_per_bank': refine_avg_ms,
+                         'launch_ms': msm_ms},
             'gpu_launches': launches_timed,
             'clocks': clocks.summary(),
             'op_ms_per_step': {k: round(v, 3) for k, v in sorted(op_ms.items(), key=lambda kv: -kv[1])},

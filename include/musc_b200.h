@@ -46,7 +46,7 @@ enum musc_b200_status {
 
 enum musc_b200_dtype { MUSC_B200_F32 = 0, MUSC_B200_F16 = 1, MUSC_B200_BF16 = 2 };
 
-/* ABI version of this header (bumped on any signature change). */
+/* ABI version of this header (bumped on any signature change): 2. */
 int musc_b200_abi_version(void);
 
 /* Thread-local message of the last failing call on this thread ("" if none). */
@@ -144,10 +144,11 @@ int musc_b200_lnamd_super_fast(const void* tokens, int dtype, int n_images,
  * ---------------------------------------------------------------------- */
 size_t musc_b200_bank_bytes(long long rows, int channels);
 
-/* Byte offsets of the bank's four planes (hi, lo, |z|^2, 2^-k) for `rows` rows.
- * The hi/lo planes hold rows * channels fp16 each and the vectors rows fp32,
- * row-contiguous, so the banks of consecutive row blocks (one per rank) are
- * gathered plane by plane into the bank of the concatenated rows. */
+/* Byte offsets of the bank's five planes (hi, lo, |z|^2, 2^-k, residual norm
+ * |lo| 2^-k) for `rows` rows: plane_offsets[0..4].  The hi/lo planes hold
+ * rows * channels fp16 each and the vectors rows fp32, row-contiguous, so the
+ * banks of consecutive row blocks (one per rank) are gathered plane by plane
+ * into the bank of the concatenated rows. */
 int musc_b200_bank_layout(long long rows, int channels, size_t* plane_offsets);
 
 /* z: [rows][channels] fp32, channels % 8 == 0.  bank: >= bank_bytes. */
@@ -199,6 +200,50 @@ int musc_b200_nearest_pool(const void* bank, long long bank_rows, long long rows
                            int patches_per_image, int part, int n_parts, long long rows_per_block,
                            int max_ctas, float* nearest_sq, musc_b200_stream stream);
 
+/* Screened pool pass: the rank-deferred form of musc_b200_nearest_pool, the
+ * default path of musc_b200_msm and musc_b200_score_pool.  Replaces the
+ * reference GPU driver's fp16 screening (models/modules/_MSM_gpu.py:739-767,
+ * deferred_half_min :307-419): the same symmetric tile list evaluated with
+ * one fp16 hi*hi MMA pass (a third of the exact path's tensor-core work).  For
+ * every (row, reference image) it stores, in the layout of
+ * musc_b200_nearest_pool ([block][image][r], blocks = ceil(rows /
+ * rows_per_block)):
+ *   k1: uint64 key (bits of the smallest screened squared distance, low 8
+ *       mantissa bits cleared) << 32 | the patch of the image attaining it;
+ *   m2: uint32 bits of the second-smallest screened squared distance over
+ *       the image's other patches (low 8 bits cleared),
+ * both 0xFF.. where unset (the call fills both first).  sched_word: 8 bytes
+ * the kernel's tile scheduler counts in.  Parts of a multi-GPU split combine
+ * through musc_b200_refine, not by a plain minimum. */
+int musc_b200_screen_pool(const void* bank, long long bank_rows, long long rows, int channels,
+                          int patches_per_image, int part, int n_parts, long long rows_per_block,
+                          int max_ctas, void* k1, void* m2, void* sched_word, musc_b200_stream stream);
+
+/* Exact minima from screened tables (the reference's rank-deferred exact
+ * evaluation, models/modules/_MSM_gpu.py:770-786: kthvalue threshold,
+ * rank_anchor_rows, rank_candidates, rank_finish).  For the query rows
+ * [first_row, first_row + query_rows) of the pool bank (all `rows` rows
+ * gathered, laid out for bank_rows), with n_partials screen tables (partial g
+ * at k1 + g * partial_stride entries, likewise m2, each [n_images][table_rows],
+ * local row index = row - first_row), writes exact_sq[n_images][query_rows]:
+ *   - FLT_MAX for the query's own image and for images whose certified lower
+ *     bound lies above the rank_hi-th smallest certified upper bound (they
+ *     cannot reach the trimmed ranks [.., rank_hi));
+ *   - the exact squared minimum (fp32-class, as musc_b200_nearest_pool) for
+ *     every other image: the exact distance to the screened argmin when the
+ *     second-smallest screened value rules out every other patch, else the
+ *     exact 3-pass minimum over the image's patches.
+ * So musc_b200_trimmed_mean over exact_sq gives the reference's scores for any
+ * rank_lo < rank_hi.  Scratch in `workspace` (musc_b200_refine_bytes, 1024-
+ * byte aligned). */
+size_t musc_b200_refine_bytes(int n_images, long long query_rows, int channels);
+
+int musc_b200_refine(const void* bank, long long bank_rows, long long rows, int channels,
+                     int patches_per_image, long long first_row, long long query_rows, int rank_hi,
+                     const void* k1, const void* m2, int n_partials, long long partial_stride,
+                     long long table_rows, float* exact_sq, void* workspace, size_t workspace_bytes,
+                     musc_b200_stream stream);
+
 /* Interval average: scores[q] = mean of ranks [rank_lo, rank_hi) of
  * sqrt(nearest_sq[:, q]) over the n_images - 1 other images, in float32,
  * stored as float64 (_MSM.py:19-30).  0 <= rank_lo < rank_hi <= n_images-1.
@@ -208,8 +253,10 @@ int musc_b200_nearest_pool(const void* bank, long long bank_rows, long long rows
 int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
                            int rank_lo, int rank_hi, double* scores, musc_b200_stream stream);
 
-/* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64.
- * The workspace holds the bank and the nearest table.  n <= 1790 (the
+/* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64: bank
+ * prep, screened pool pass, refinement to exact minima, interval average
+ * (MUSC_B200_MSM_EXACT=1 in the environment: the 3-pass musc_b200_nearest_pool
+ * instead of screen + refinement).  The workspace holds the bank and the tables.  n <= 1790 (the
  * interval average's shared-memory limit, see musc_b200_trimmed_mean). */
 size_t musc_b200_msm_workspace_bytes(int n, int p, int c);
 

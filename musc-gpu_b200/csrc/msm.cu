@@ -25,6 +25,7 @@
 //      for m = rank_hi and rank_lo; score = mean of ranks [rank_lo, rank_hi)
 //      rounded to fp32 like the reference's fp32 mean, stored as float64.
 #include "common.cuh"
+#include "nearest.cuh"
 #include "tc.cuh"
 
 #include <algorithm>
@@ -35,16 +36,25 @@
 
 namespace musc {
 
+// Implemented in refine.cu.
+size_t refine_workspace_bytes(int n_images, long long q_rows, int channels);
+int refine_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
+                  long long first_row, long long q_rows, int rank_hi, const unsigned long long* k1,
+                  const unsigned int* m2, int n_parts, long long part_stride, long long table_rows,
+                  float* exact, void* workspace, cudaStream_t s);
+
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct BankLayout {
-  size_t hi, lo, norm, inv, total;
+  size_t hi, lo, norm, inv, lnorm, total;
 };
 
+// Planes: hi, lo (fp16 [rows][C]), |z|^2, 2^-k and the residual norm |lo| 2^-k (fp32 [rows]),
+// each 1024-byte aligned.
 static BankLayout bank_layout(long long rows, int channels) {
   const size_t plane = align_up((size_t)rows * channels * 2, 1024);
   const size_t vec = align_up((size_t)rows * 4, 1024);
-  return {0, plane, 2 * plane, 2 * plane + vec, 2 * plane + 2 * vec};
+  return {0, plane, 2 * plane, 2 * plane + vec, 2 * plane + 2 * vec, 2 * plane + 3 * vec};
 }
 
 // ------------------------------------------------------------------ prep
@@ -52,7 +62,8 @@ constexpr int kPrepWarps = 8;
 
 __global__ void __launch_bounds__(kPrepWarps * 32)
 prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __half* __restrict__ hi,
-                 __half* __restrict__ lo, float* __restrict__ norm2, float* __restrict__ inv_scale) {
+                 __half* __restrict__ lo, float* __restrict__ norm2, float* __restrict__ inv_scale,
+                 float* __restrict__ lo_norm) {
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
   if (row >= rows) return;  // warp-uniform
@@ -74,6 +85,7 @@ prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __ha
   const float s = ldexpf(1.f, k);
   __half* hr = hi + row * channels;
   __half* lr = lo + row * channels;
+  double ll = 0.0;
   for (int c = lane * 4; c < channels; c += 128) {
     float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
     const float x[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
@@ -82,6 +94,8 @@ prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __ha
     for (int e = 0; e < 4; ++e) {
       h[e] = __float2half_rn(x[e]);
       l[e] = __float2half_rn(x[e] - __half2float(h[e]));
+      const double le = (double)__half2float(l[e]);
+      ll += le * le;
     }
     uint2 ph, pl;
     __half2 t;
@@ -92,563 +106,18 @@ prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __ha
     *reinterpret_cast<uint2*>(hr + c) = ph;
     *reinterpret_cast<uint2*>(lr + c) = pl;
   }
+  ll = warp_sum(ll);
   if (lane == 0) {
     norm2[row] = (float)ss;
     inv_scale[row] = ldexpf(1.f, -k);
+    // Residual norm |z 2^k - hi| in original units, rounded up, for the screen's error
+    // bound: lo carries z 2^k - hi to fp16 rounding (relative 2^-11, absolute 2^-25 for
+    // subnormal lo), so |z 2^k - hi| <= |lo| (1 + 2^-10) + sqrt(C) 2^-24.
+    lo_norm[row] = (float)((sqrt(ll) * (1.0 + 0x1p-10) + sqrt((double)channels) * 0x1p-24) * (1.0 + 1.0e-6)) *
+                   ldexpf(1.f, -k);
   }
 }
 
-// ------------------------------------------------------------------ nearest
-namespace nearest {
-constexpr int CTA_M = 128;        // query rows per CTA (TMEM lanes)
-constexpr int BN = 256;           // reference rows per tile (TMEM columns per accumulator)
-constexpr int BK = 32;            // fp16 elements per K slice = one 64-byte swizzle row
-constexpr int A_BYTES = CTA_M * BK * 2;  // 8 KB per plane
-constexpr int NUM_ACC = 2;
-constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
-constexpr int EPI_WARPS = 4;
-constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr uint64_t WAIT_LIMIT_NS = 4000000000ull;  // 4 s per wait
-constexpr float INF = FLT_MAX;
-constexpr int RING = 8;      // tile indices handed from the producer to the MMA and epilogue warps
-constexpr int CHUNK = 8;     // tiles claimed per atomic by the dynamic scheduler
-
-// Tile shapes.  Single CTA: 128 x 256 tiles, the CTA holds all 256 B rows of
-// a K slice.  CTA pair (cta_group::2): 256 x 256 tiles over two SMs; each CTA
-// loads 128 A rows and 128 B rows, so per MMA an SM reads 8 KB of operands
-// from shared memory instead of 12 KB and fetches a third fewer bytes from
-// L2, and the smaller stages allow a 6-deep ring in the same shared memory.
-template <bool PAIR>
-struct Cfg {
-  static constexpr int TILE_M = PAIR ? 256 : 128;
-  static constexpr int CTA_N = PAIR ? 128 : 256;
-  static constexpr int B_BYTES = CTA_N * BK * 2;
-  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 48 KB / 32 KB
-  static constexpr int STAGES = PAIR ? 6 : 4;
-  static constexpr int GROUP_M = PAIR ? 32 : 64;  // m-tiles swept together (8192 query rows)
-  static constexpr uint32_t IDESC = tc::idesc_f16(TILE_M, BN, /*fp16*/ 0);
-  static constexpr int EPI_ARRIVALS = (PAIR ? 2 : 1) * EPI_WARPS;  // epilogue warps releasing a tile
-};
-
-template <int STAGES, int STAGE_BYTES>
-struct Smem {
-  uint8_t tiles[STAGES][STAGE_BYTES];  // 1024-aligned base
-  float col_norm[BN];
-  float col_w[BN];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t acc_full[NUM_ACC];
-  uint64_t acc_empty[NUM_ACC];
-  uint64_t drain;
-  uint64_t ring_full[RING];
-  uint64_t ring_empty[RING];
-  long long tile_ring[RING];
-  uint32_t tmem_base;
-  int abort_flag;
-};
-template <bool PAIR>
-using SmemT = Smem<Cfg<PAIR>::STAGES, Cfg<PAIR>::STAGE_BYTES>;
-template <bool PAIR>
-constexpr size_t smem_bytes() {
-  return sizeof(SmemT<PAIR>) + 1024;
-}
-
-struct Params {
-  const float* q_norm;
-  const float* q_inv;
-  const float* r_norm;
-  const float* r_inv;
-  unsigned int* nearest;  // float bits, layout [row / rpb][image][row % rpb]
-  unsigned long long* sched;  // dynamic-scheduler counter (zeroed before the launch), or nullptr
-  int* err;
-  long long q_rows, r_rows, q_first_row;
-  long long tile_begin, tile_end;  // linear tile range processed by this launch
-  long long rows_per_block;        // rpb of the nearest layout
-  int blocked;                     // 0: rows_per_block covers every row addressed
-  int patches;                     // P
-  int n_images;
-  int num_kb;
-  int num_m, num_n;
-};
-
-__host__ __device__ inline void tile_coords(long long tile, int num_m, int num_n, int group_m, int* m_blk,
-                                            int* n_blk) {
-  const long long group = tile / ((long long)group_m * num_n);
-  const int first_m = (int)(group * group_m);
-  const int gm = num_m - first_m < group_m ? num_m - first_m : group_m;
-  const long long local = tile - group * group_m * (long long)num_n;
-  *m_blk = first_m + (int)(local % gm);
-  *n_blk = (int)(local / gm);
-}
-
-// Symmetric mode: tile (m, n) holds an element (r, c) with img(r) < img(c).
-__host__ __device__ inline bool sym_needed(int m, int n, long long rows, int patches, int n_images, int tile_m) {
-  const long long r0 = (long long)m * tile_m;
-  const long long img_r = r0 / patches;
-  if (img_r >= n_images - 1) return false;
-  long long c_last = (long long)n * BN + BN - 1;
-  if (c_last > rows - 1) c_last = rows - 1;
-  return c_last / patches > img_r;
-}
-
-// Bounded wait: true when the phase completed; false after the time limit
-// (which raises this CTA's abort flag, the peer CTA's when `peer_abort` is a
-// cluster address, and the device error word) or when an abort was already
-// raised.  CLUSTER selects acquire at cluster scope, for phases completed by
-// the other CTA of a pair.
-template <bool CLUSTER>
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                             uint32_t peer_abort) {
-  auto ready = [&]() { return CLUSTER ? tc::mbar_try_wait_cluster(bar, parity) : tc::mbar_try_wait(bar, parity); };
-  if (ready()) return true;
-  const uint64_t start = global_ns();
-  uint32_t iter = 0;
-  while (true) {
-    if (ready()) return true;
-    if ((++iter & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - start > WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        if (peer_abort) tc::st_cluster_u32(peer_abort, 1u);
-        atomicExch(err, MUSC_B200_ERR_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void named_sync_epi() {
-  asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
-}
-
-// Barrier over the epilogue warps that also ORs `flag` across them, so every
-// epilogue thread takes the same branch afterwards.
-__device__ __forceinline__ bool named_sync_epi_any(int flag) {
-  uint32_t res;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(res)
-      : "r"(flag), "n"(EPI_WARPS * 32)
-      : "memory");
-  return res != 0;
-}
-
-__device__ __forceinline__ long long table_index(const Params& p, int img, long long row) {
-  if (!p.blocked) return (long long)img * p.rows_per_block + row;
-  const long long blk = row / p.rows_per_block;
-  return (blk * p.n_images + img) * p.rows_per_block + (row - blk * p.rows_per_block);
-}
-
-__device__ __forceinline__ void flush_min(const Params& p, long long row, int img, float m) {
-  if (m < INF) {
-    const float v = m > 0.f ? m : 0.f;
-    atomicMin(p.nearest + table_index(p, img, row), __float_as_uint(v));
-  }
-}
-
-// After the call lane l holds min over the warp's 32 lanes of v[l] (a
-// transposing butterfly: 31 shuffles for 32 columns).
-__device__ __forceinline__ float warp_column_min(float (&v)[32], int lane) {
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) {
-    const bool upper = (lane & s) != 0;
-#pragma unroll
-    for (int i = 0; i < s; ++i) {
-      const float send = upper ? v[i] : v[i + s];
-      const float keep = upper ? v[i + s] : v[i];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
-      v[i] = fminf(keep, recv);
-    }
-  }
-  return v[0];
-}
-
-// Roles (one CTA, or each CTA of a pair): warp 0 lane 0 loads (TMA), warp 1
-// lane 0 issues the MMAs (the even CTA only, for a pair), warps 2-5 are the
-// epilogue.  In a pair the even CTA (rank 0) owns the schedule: its producer
-// claims each tile, writes the index into both CTAs' rings and both CTAs'
-// loads complete on its `full` barriers; its MMA thread signals both CTAs'
-// `empty` and `acc_full` barriers; both epilogues release the accumulator and
-// the ring slot on its barriers.
-template <bool SYM, bool PAIR>
-__global__ void __launch_bounds__(THREADS, 1)
-nearest_kernel(const __grid_constant__ CUtensorMap map_q_hi, const __grid_constant__ CUtensorMap map_q_lo,
-               const __grid_constant__ CUtensorMap map_r_hi, const __grid_constant__ CUtensorMap map_r_lo,
-               const Params p) {
-  using C = Cfg<PAIR>;
-  extern __shared__ uint8_t smem_raw[];
-  SmemT<PAIR>& sm =
-      *reinterpret_cast<SmemT<PAIR>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  volatile int* abort_flag = &sm.abort_flag;
-  const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
-  const bool leader = rank == 0;
-  const uint32_t peer_abort = PAIR ? tc::mapa(tc::smem_u32(&sm.abort_flag), rank ^ 1u) : 0u;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      tc::mbar_init(tc::smem_u32(&sm.full[s]), 1);
-      tc::mbar_init(tc::smem_u32(&sm.empty[s]), 1);
-    }
-    for (int a = 0; a < NUM_ACC; ++a) {
-      tc::mbar_init(tc::smem_u32(&sm.acc_full[a]), 1);
-      tc::mbar_init(tc::smem_u32(&sm.acc_empty[a]), C::EPI_ARRIVALS);
-    }
-    tc::mbar_init(tc::smem_u32(&sm.drain), 1);
-    for (int i = 0; i < RING; ++i) {
-      tc::mbar_init(tc::smem_u32(&sm.ring_full[i]), 1);
-      tc::mbar_init(tc::smem_u32(&sm.ring_empty[i]), C::EPI_ARRIVALS);
-    }
-    sm.abort_flag = 0;
-    tc::fence_barrier_init();
-    tc::prefetch_tensormap(&map_q_hi);
-    tc::prefetch_tensormap(&map_q_lo);
-    tc::prefetch_tensormap(&map_r_hi);
-    tc::prefetch_tensormap(&map_r_lo);
-  }
-  if (warp == 1) {
-    if (PAIR) {
-      tc::tmem_alloc_pair(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
-      tc::tmem_relinquish_pair();
-    } else {
-      tc::tmem_alloc(tc::smem_u32(&sm.tmem_base), TMEM_COLS);
-      tc::tmem_relinquish();
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  if (PAIR) tc::cluster_sync();  // the peer's barriers exist before anything arrives on them
-  tc::fence_after_sync();
-  const uint32_t tmem_base = sm.tmem_base;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_phase[C::STAGES];
-      bool issued[C::STAGES];
-      for (int s = 0; s < C::STAGES; ++s) issued[s] = false, issued_phase[s] = 0;
-      bool ok = true;
-      const long long group_id = PAIR ? (long long)tc::cluster_id_x() : (long long)blockIdx.x;
-      const long long n_groups = PAIR ? (long long)tc::cluster_count_x() : (long long)gridDim.x;
-      long long next_static = p.tile_begin + group_id, chunk_cur = 0, chunk_end = 0;
-      // Next tile (linear index), or -1.  Static: stride = number of CTAs (pairs).
-      // Dynamic: claim CHUNK consecutive indices per atomic, so CTAs that start late
-      // (their SM busy with another kernel, e.g. a collective) simply take fewer.
-      auto next_tile = [&]() -> long long {
-        while (true) {
-          long long t;
-          if (p.sched) {
-            if (chunk_cur >= chunk_end) {
-              const long long c = (long long)atomicAdd(p.sched, 1ull);
-              chunk_cur = p.tile_begin + c * CHUNK;
-              chunk_end = chunk_cur + CHUNK < p.tile_end ? chunk_cur + CHUNK : p.tile_end;
-              if (chunk_cur >= p.tile_end) return -1;
-            }
-            t = chunk_cur++;
-          } else {
-            t = next_static;
-            if (t >= p.tile_end) return -1;
-            next_static += n_groups;
-          }
-          if (!SYM) return t;
-          int mb, nb;
-          tile_coords(t, p.num_m, p.num_n, C::GROUP_M, &mb, &nb);
-          if (sym_needed(mb, nb, p.r_rows, p.patches, p.n_images, C::TILE_M)) return t;
-        }
-      };
-      for (int local = 0; ok; ++local) {
-        const int slot = local % RING;
-        const uint32_t ring_parity = (uint32_t)(local / RING) & 1u;
-        long long tile;
-        if (leader) {
-          if (!wait_bounded<PAIR>(tc::smem_u32(&sm.ring_empty[slot]), ring_parity ^ 1u, abort_flag, p.err,
-                                  peer_abort)) {
-            ok = false;
-            break;
-          }
-          tile = next_tile();
-          sm.tile_ring[slot] = tile;
-          if (PAIR) {
-            tc::st_cluster_s64(tc::mapa(tc::smem_u32(&sm.tile_ring[slot]), 1u), tile);
-            tc::mbar_arrive_cluster(tc::mapa(tc::smem_u32(&sm.ring_full[slot]), 1u));
-          }
-          tc::mbar_arrive(tc::smem_u32(&sm.ring_full[slot]));
-        } else {
-          if (!wait_bounded<true>(tc::smem_u32(&sm.ring_full[slot]), ring_parity, abort_flag, p.err, peer_abort)) {
-            ok = false;
-            break;
-          }
-          tile = sm.tile_ring[slot];
-        }
-        if (tile < 0) break;
-        int m_blk, n_blk;
-        tile_coords(tile, p.num_m, p.num_n, C::GROUP_M, &m_blk, &n_blk);
-        const int a_row = m_blk * C::TILE_M + (int)rank * CTA_M;
-        const int b_row = n_blk * BN + (int)rank * C::CTA_N;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bounded<false>(tc::smem_u32(&sm.empty[stage]), phase ^ 1, abort_flag, p.err, peer_abort)) {
-            ok = false;
-            break;
-          }
-          const uint32_t full_local = tc::smem_u32(&sm.full[stage]);
-          // The leader's barrier counts both CTAs' bytes of this stage.
-          if (leader) tc::mbar_arrive_expect_tx(full_local, (PAIR ? 2 : 1) * C::STAGE_BYTES);
-          const uint32_t base = tc::smem_u32(sm.tiles[stage]);
-          const int kc = kb * BK;
-          if (PAIR) {
-            const uint32_t full = tc::mapa(full_local, 0u);
-            tc::tma_load_2d_pair(base, &map_q_hi, kc, a_row, full);
-            tc::tma_load_2d_pair(base + A_BYTES, &map_q_lo, kc, a_row, full);
-            tc::tma_load_2d_pair(base + 2 * A_BYTES, &map_r_hi, kc, b_row, full);
-            tc::tma_load_2d_pair(base + 2 * A_BYTES + C::B_BYTES, &map_r_lo, kc, b_row, full);
-          } else {
-            tc::tma_load_2d(base, &map_q_hi, kc, a_row, full_local);
-            tc::tma_load_2d(base + A_BYTES, &map_q_lo, kc, a_row, full_local);
-            tc::tma_load_2d(base + 2 * A_BYTES, &map_r_hi, kc, b_row, full_local);
-            tc::tma_load_2d(base + 2 * A_BYTES + C::B_BYTES, &map_r_lo, kc, b_row, full_local);
-          }
-          issued[stage] = true;
-          issued_phase[stage] = phase;
-          if (++stage == C::STAGES) stage = 0, phase ^= 1;
-        }
-      }
-      if (!ok) {
-        // Let the copies already in flight land before the CTA exits.  The
-        // leader watches its `full` barriers (one deadline for all stages); the
-        // peer's copies complete on the leader's barriers, so it gives them a
-        // fixed 2 ms, far above the latency of one copy.
-        const uint64_t start = global_ns();
-        if (leader) {
-          for (int s = 0; s < C::STAGES; ++s) {
-            if (!issued[s]) continue;
-            while (!tc::mbar_try_wait(tc::smem_u32(&sm.full[s]), issued_phase[s]) &&
-                   global_ns() - start < WAIT_LIMIT_NS) {
-            }
-          }
-        } else {
-          while (global_ns() - start < 2000000ull) {
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0 && leader) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      bool ok = true;
-      for (int local = 0; ok; ++local) {
-        const int slot = local % RING;
-        if (!wait_bounded<false>(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u, abort_flag,
-                                 p.err, peer_abort)) {
-          ok = false;
-          break;
-        }
-        if (sm.tile_ring[slot] < 0) break;
-        if (!wait_bounded<PAIR>(tc::smem_u32(&sm.acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, peer_abort)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bounded<false>(tc::smem_u32(&sm.full[stage]), phase, abort_flag, p.err, peer_abort)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_sync();
-          const uint32_t base = tc::smem_u32(sm.tiles[stage]);
-#pragma unroll
-          for (int k16 = 0; k16 < BK / 16; ++k16) {
-            const uint32_t koff = (uint32_t)(k16 * 32);  // 16 fp16 = 32 bytes along the swizzled row
-            const uint64_t a_hi = tc::desc_k_sw64(base + koff);
-            const uint64_t a_lo = tc::desc_k_sw64(base + A_BYTES + koff);
-            const uint64_t b_hi = tc::desc_k_sw64(base + 2 * A_BYTES + koff);
-            const uint64_t b_lo = tc::desc_k_sw64(base + 2 * A_BYTES + C::B_BYTES + koff);
-            const uint32_t first = (kb | k16) != 0 ? 1u : 0u;
-            if (PAIR) {
-              tc::mma_f16_ss_pair(d_tmem, a_hi, b_hi, C::IDESC, first);
-              tc::mma_f16_ss_pair(d_tmem, a_hi, b_lo, C::IDESC, 1u);
-              tc::mma_f16_ss_pair(d_tmem, a_lo, b_hi, C::IDESC, 1u);
-            } else {
-              tc::mma_f16_ss(d_tmem, a_hi, b_hi, C::IDESC, first);
-              tc::mma_f16_ss(d_tmem, a_hi, b_lo, C::IDESC, 1u);
-              tc::mma_f16_ss(d_tmem, a_lo, b_hi, C::IDESC, 1u);
-            }
-          }
-          const uint32_t empty = tc::smem_u32(&sm.empty[stage]);
-          if (PAIR) {
-            tc::mma_commit_pair(empty);
-            tc::mma_commit_pair(tc::mapa(empty, 1u));
-          } else {
-            tc::mma_commit(empty);
-          }
-          if (++stage == C::STAGES) stage = 0, phase ^= 1;
-        }
-        if (!ok) break;
-        const uint32_t accf = tc::smem_u32(&sm.acc_full[acc]);
-        if (PAIR) {
-          tc::mma_commit_pair(accf);
-          tc::mma_commit_pair(tc::mapa(accf, 1u));
-        } else {
-          tc::mma_commit(accf);
-        }
-        if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
-      }
-      if (!ok) {
-        // Wait for this thread's MMAs in flight before TMEM is released.
-        if (PAIR) tc::mma_commit_pair(tc::smem_u32(&sm.drain));
-        else tc::mma_commit(tc::smem_u32(&sm.drain));
-        const uint64_t start = global_ns();
-        while (!tc::mbar_try_wait(tc::smem_u32(&sm.drain), 0) && global_ns() - start < WAIT_LIMIT_NS) {
-        }
-      }
-    }
-  } else {
-    // ---------------------------------------------------------- epilogue
-    const int et = threadIdx.x - 64;         // 0..127
-    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int P = p.patches;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int local = 0;; ++local) {
-      const int slot = local % RING;
-      const bool got = wait_bounded<PAIR>(tc::smem_u32(&sm.ring_full[slot]), (uint32_t)(local / RING) & 1u,
-                                          abort_flag, p.err, peer_abort);
-      const long long tile = got ? sm.tile_ring[slot] : -1;
-      if (named_sync_epi_any(tile < 0)) break;  // uniform: every epilogue thread read the same slot
-      int m_blk, n_blk;
-      tile_coords(tile, p.num_m, p.num_n, C::GROUP_M, &m_blk, &n_blk);
-      const long long n0 = (long long)n_blk * BN;
-      named_sync_epi();  // previous tile's readers are done with col_norm / col_w
-      for (int j = et; j < BN; j += EPI_WARPS * 32) {
-        const long long col = n0 + j;
-        const bool ok = col < p.r_rows;
-        sm.col_norm[j] = ok ? __ldg(p.r_norm + col) : 0.f;
-        sm.col_w[j] = ok ? 2.f * __ldg(p.r_inv + col) : 0.f;
-      }
-      wait_bounded<false>(tc::smem_u32(&sm.acc_full[acc]), acc_phase, abort_flag, p.err, peer_abort);
-      if (named_sync_epi_any(*abort_flag)) break;  // uniform decision across the epilogue warps
-      tc::fence_after_sync();
-
-      const long long cta_row0 = (long long)m_blk * C::TILE_M + (long long)rank * CTA_M;
-      const long long warp_row0 = cta_row0 + quarter * 32;
-      const long long row = warp_row0 + lane;
-      const bool row_ok = row < p.q_rows;
-      const float qn = row_ok ? __ldg(p.q_norm + row) : 0.f;
-      const float qi = row_ok ? __ldg(p.q_inv + row) : 0.f;
-      const int q_img = (int)((p.q_first_row + row) / P);
-      // Symmetric mode keeps only columns of a later image than the row's.
-      const long long col_from = SYM ? (long long)(q_img + 1) * P : 0;
-      long long cta_last_row = cta_row0 + CTA_M - 1;
-      if (cta_last_row > p.q_rows - 1) cta_last_row = p.q_rows - 1;
-      const bool rows_full = cta_row0 + CTA_M <= p.q_rows;
-      const bool clean = !SYM || (rows_full && (cta_last_row / P) < (n0 / P));
-      // row images covered by this warp (symmetric column minima)
-      const bool warp_any = warp_row0 < p.q_rows;
-      long long warp_last = warp_row0 + 31;
-      if (warp_last > p.q_rows - 1) warp_last = p.q_rows - 1;
-      const int w_img0 = (int)(warp_row0 / P), w_img1 = warp_any ? (int)(warp_last / P) : w_img0 - 1;
-
-      int seg_img = (int)(n0 / P);
-      long long seg_end = (long long)(seg_img + 1) * P;
-      float m = INF;
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
-        const long long c0 = n0 + chunk * 32;
-        if (c0 >= p.r_rows) break;
-        uint32_t raw[32];
-        tc::tmem_ld_32x32b_x32(tbase + (uint32_t)(chunk * 32), raw);
-        tc::tmem_wait_ld();
-        float v[32];
-        const bool full_chunk = c0 + 32 <= p.r_rows;
-        if (clean && full_chunk) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int jj = chunk * 32 + j;
-            v[j] = fmaf(-__uint_as_float(raw[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int jj = chunk * 32 + j;
-            const long long col = c0 + j;
-            const bool ok = row_ok && col < p.r_rows && col >= col_from;
-            v[j] = ok ? fmaf(-__uint_as_float(raw[j]), qi * sm.col_w[jj], qn + sm.col_norm[jj]) : INF;
-          }
-        }
-        // Row minima per reference-image segment.
-        if (c0 + 32 <= seg_end) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) m = fminf(m, v[j]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j >= seg_end) {
-              if (row_ok && seg_img != q_img) flush_min(p, row, seg_img, m);
-              ++seg_img;
-              seg_end += P;
-              m = INF;
-            }
-            m = fminf(m, v[j]);
-          }
-        }
-        if (SYM) {
-          // Column minima over this warp's rows, one per row image.
-          const long long col = c0 + lane;
-          if (w_img0 == w_img1) {
-            const float cm = warp_column_min(v, lane);
-            if (col < p.r_rows) flush_min(p, col, w_img0, cm);
-          } else {
-            for (int ri = w_img0; ri <= w_img1; ++ri) {
-              float u[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) u[j] = (q_img == ri) ? v[j] : INF;
-              const float cm = warp_column_min(u, lane);
-              if (col < p.r_rows) flush_min(p, col, ri, cm);
-            }
-          }
-        }
-      }
-      if (row_ok && seg_img != q_img) flush_min(p, row, seg_img, m);
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        const uint32_t acc_e = tc::smem_u32(&sm.acc_empty[acc]);
-        const uint32_t ring_e = tc::smem_u32(&sm.ring_empty[slot]);
-        if (leader) {
-          tc::mbar_arrive(acc_e);
-          tc::mbar_arrive(ring_e);
-        } else {
-          tc::mbar_arrive_cluster(tc::mapa(acc_e, 0u));
-          tc::mbar_arrive_cluster(tc::mapa(ring_e, 0u));
-        }
-      }
-      if (++acc == NUM_ACC) acc = 0, acc_phase ^= 1;
-    }
-  }
-
-  tc::fence_before_sync();
-  __syncthreads();
-  if (PAIR) tc::cluster_sync();  // no access to the other CTA's shared memory or TMEM is still pending
-  if (warp == 1) {
-    tc::fence_after_sync();
-    if (PAIR) tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
-    else tc::tmem_dealloc(tmem_base, TMEM_COLS);
-  }
-  if (PAIR) tc::cluster_sync();
-}
-
-}  // namespace nearest
 
 // ------------------------------------------------------------------ fill
 __global__ void fill_u32_kernel(unsigned int* p, long long n, unsigned int v) {
@@ -781,21 +250,6 @@ int get_encode_fn(EncodeTiledFn* fn) {
   return MUSC_B200_OK;
 }
 
-// 2-D fp16 plane [rows][channels], box = 32 channels x box_rows, 64-byte swizzle.
-int make_plane_map(CUtensorMap* map, const void* base, long long rows, int channels, int box_rows) {
-  EncodeTiledFn encode;
-  MUSC_TRY(get_encode_fn(&encode));
-  cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
-  cuuint32_t box[2] = {(cuuint32_t)nearest::BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(MUSC_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
-  return MUSC_B200_OK;
-}
-
 int check_bank_args(long long rows, int channels) {
   if (rows <= 0 || channels <= 0) return fail(MUSC_B200_ERR_INVALID, "bank: requires rows > 0, channels > 0");
   if (channels % 8 != 0) return fail(MUSC_B200_ERR_INVALID, "bank: channels must be a multiple of 8");
@@ -806,6 +260,24 @@ int check_bank_args(long long rows, int channels) {
 int trimmed_pitch(int n) { return n + (((4 - n) % 32) + 32) % 32; }  // >= n, == 4 (mod 32)
 
 }  // namespace
+
+// 2-D fp16 plane [rows][channels], box = k_box channels x box_rows; k_box 32 (64-byte rows,
+// 64-byte swizzle) or 64 (128-byte rows, 128-byte swizzle).
+int make_plane_map(CUtensorMap* map, const void* base, long long rows, int channels, int box_rows, int k_box) {
+  EncodeTiledFn encode;
+  MUSC_TRY(get_encode_fn(&encode));
+  if (k_box != 32 && k_box != 64) return fail(MUSC_B200_ERR_INVALID, "make_plane_map: k_box must be 32 or 64");
+  cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
+  cuuint32_t box[2] = {(cuuint32_t)k_box, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      k_box == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MUSC_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return MUSC_B200_OK;
+}
 
 // Balanced split of the symmetric tile list.  Tiles are visited in the
 // kernel's linear order (groups of GROUP_M m-tiles, n outer, m inner); the
@@ -852,27 +324,37 @@ static void sym_part_range(long long rows, int patches, int n_images, int num_m,
   *tile_end = start_of(part + 1);
 }
 
-static int set_smem_attr() {
+template <int MODE, bool PAIR>
+static int set_attr_one() {
+  return cudaFuncSetAttribute(nearest::nearest_kernel<MODE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)nearest::smem_bytes<MODE, PAIR>()) == cudaSuccess
+             ? MUSC_B200_OK
+             : fail(MUSC_B200_ERR_CUDA, "cudaFuncSetAttribute(nearest_kernel) failed");
+}
+
+// Opt every instantiation of the nearest kernel in to its shared memory (once per device).
+int set_nearest_smem_attrs() {
   static std::mutex m;
   static bool done[64] = {false};
   int dev = 0;
   MUSC_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lock(m);
   if (dev >= 64 || !done[dev]) {
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<false, false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<false>()));
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true, false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<false>()));
-    MUSC_CUDA(cudaFuncSetAttribute(nearest::nearest_kernel<true, true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nearest::smem_bytes<true>()));
+    using namespace nearest;
+    MUSC_TRY((set_attr_one<DIRECTED, false>()));
+    MUSC_TRY((set_attr_one<SYM, false>()));
+    MUSC_TRY((set_attr_one<SYM, true>()));
+    MUSC_TRY((set_attr_one<SCREEN, false>()));
+    MUSC_TRY((set_attr_one<SCREEN, true>()));
+    MUSC_TRY((set_attr_one<GATHER, false>()));
     if (dev < 64) done[dev] = true;
   }
   return MUSC_B200_OK;
 }
 
-// The symmetric pool kernel runs as CTA pairs (cta_group::2) unless
-// MUSC_B200_NEAREST_PAIR=0 selects the single-CTA kernel; both compute the
-// same table bit for bit.
+// The symmetric pool kernels run as CTA pairs (cta_group::2) unless
+// MUSC_B200_NEAREST_PAIR=0 selects the single-CTA kernels; both compute the
+// same tables bit for bit.
 static bool use_cta_pairs() {
   const char* e = std::getenv("MUSC_B200_NEAREST_PAIR");
   return !(e && e[0] == '0');
@@ -886,18 +368,19 @@ static int fill_table(float* table, long long count, cudaStream_t s) {
 int nearest_launch(const void* query_bank, long long query_rows, long long query_first_row,
                    const void* ref_bank, long long ref_rows, int channels, int patches,
                    float* nearest_sq, cudaStream_t s) {
+  using namespace nearest;
   const BankLayout ql = bank_layout(query_rows, channels);
   const BankLayout rl = bank_layout(ref_rows, channels);
   const uint8_t* qb = static_cast<const uint8_t*>(query_bank);
   const uint8_t* rb = static_cast<const uint8_t*>(ref_bank);
   CUtensorMap mqh, mql, mrh, mrl;
-  MUSC_TRY(make_plane_map(&mqh, qb + ql.hi, query_rows, channels, nearest::CTA_M));
-  MUSC_TRY(make_plane_map(&mql, qb + ql.lo, query_rows, channels, nearest::CTA_M));
-  MUSC_TRY(make_plane_map(&mrh, rb + rl.hi, ref_rows, channels, nearest::BN));
-  MUSC_TRY(make_plane_map(&mrl, rb + rl.lo, ref_rows, channels, nearest::BN));
+  MUSC_TRY(make_plane_map(&mqh, qb + ql.hi, query_rows, channels, CTA_M, BK));
+  MUSC_TRY(make_plane_map(&mql, qb + ql.lo, query_rows, channels, CTA_M, BK));
+  MUSC_TRY(make_plane_map(&mrh, rb + rl.hi, ref_rows, channels, BN, BK));
+  MUSC_TRY(make_plane_map(&mrl, rb + rl.lo, ref_rows, channels, BN, BK));
   const int n_images = (int)(ref_rows / patches);
   MUSC_TRY(fill_table(nearest_sq, (long long)n_images * query_rows, s));
-  nearest::Params p;
+  Params p{};
   p.q_norm = reinterpret_cast<const float*>(qb + ql.norm);
   p.q_inv = reinterpret_cast<const float*>(qb + ql.inv);
   p.r_norm = reinterpret_cast<const float*>(rb + rl.norm);
@@ -912,67 +395,58 @@ int nearest_launch(const void* query_bank, long long query_rows, long long query
   p.blocked = 0;
   p.patches = patches;
   p.n_images = n_images;
-  p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
-  p.num_m = (int)((query_rows + nearest::CTA_M - 1) / nearest::CTA_M);
-  p.num_n = (int)((ref_rows + nearest::BN - 1) / nearest::BN);
+  p.num_kb = (channels + BK - 1) / BK;
+  p.num_m = (int)((query_rows + CTA_M - 1) / CTA_M);
+  p.num_n = (int)((ref_rows + BN - 1) / BN);
   p.tile_begin = 0;
   p.tile_end = (long long)p.num_m * p.num_n;
   p.sched = nullptr;  // static schedule
-  MUSC_TRY(set_smem_attr());
+  MUSC_TRY(set_nearest_smem_attrs());
   const int grid = (int)std::min<long long>(p.tile_end, sm_count());
-  nearest::nearest_kernel<false, false><<<grid, nearest::THREADS, nearest::smem_bytes<false>(), s>>>(
+  nearest_kernel<DIRECTED, false><<<grid, Cfg<DIRECTED, false>::THREADS, smem_bytes<DIRECTED, false>(), s>>>(
       mqh, mql, mrh, mrl, p);
   return check_launch("nearest_kernel<directed>");
 }
 
-int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
-                        int part, int parts, long long rows_per_block, int max_ctas, float* nearest_sq,
-                        cudaStream_t s) {
+// Launch a symmetric pool kernel (SYM or SCREEN) over part `part` of `parts` of the
+// tile list; p holds the outputs, the caller has filled them.
+template <int MODE>
+static int pool_kernel_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
+                              int part, int parts, int max_ctas, nearest::Params& p, cudaStream_t s) {
+  using namespace nearest;
   const BankLayout l = bank_layout(bank_rows, channels);
   const uint8_t* b = static_cast<const uint8_t*>(bank);
   const bool pair = use_cta_pairs();
-  const int b_box = pair ? nearest::Cfg<true>::CTA_N : nearest::Cfg<false>::CTA_N;
+  const int b_box = pair ? Cfg<MODE, true>::CTA_N : Cfg<MODE, false>::CTA_N;
   CUtensorMap mah, mal, mbh, mbl;
-  MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, nearest::CTA_M));
-  MUSC_TRY(make_plane_map(&mal, b + l.lo, rows, channels, nearest::CTA_M));
-  MUSC_TRY(make_plane_map(&mbh, b + l.hi, rows, channels, b_box));
-  MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, b_box));
-  const int n_images = (int)(rows / patches);
-  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  const long long table = blocks * n_images * rows_per_block;
-  MUSC_TRY(fill_table(nearest_sq, table, s));
-  // The scheduler counter lives in the 256 bytes after the table (musc_b200_nearest_pool_bytes).
-  unsigned long long* sched = reinterpret_cast<unsigned long long*>(
-      reinterpret_cast<uint8_t*>(nearest_sq) + ((size_t)table * sizeof(float) + 255) / 256 * 256);
-  MUSC_CUDA(cudaMemsetAsync(sched, 0, sizeof(unsigned long long), s));
-  nearest::Params p;
+  const int kb = Cfg<MODE, false>::KB;
+  MUSC_TRY(make_plane_map(&mah, b + l.hi, rows, channels, CTA_M, kb));
+  MUSC_TRY(make_plane_map(&mal, b + l.lo, rows, channels, CTA_M, kb));
+  MUSC_TRY(make_plane_map(&mbh, b + l.hi, rows, channels, b_box, kb));
+  MUSC_TRY(make_plane_map(&mbl, b + l.lo, rows, channels, b_box, kb));
   p.q_norm = p.r_norm = reinterpret_cast<const float*>(b + l.norm);
   p.q_inv = p.r_inv = reinterpret_cast<const float*>(b + l.inv);
-  p.nearest = reinterpret_cast<unsigned int*>(nearest_sq);
-  p.sched = sched;
   p.err = device_error_ptr();
   if (!p.err) return fail(MUSC_B200_ERR_CUDA, "nearest_pool: device error word unavailable");
   p.q_rows = p.r_rows = rows;
   p.q_first_row = 0;
-  p.rows_per_block = rows_per_block;
-  p.blocked = blocks > 1 ? 1 : 0;
   p.patches = patches;
-  p.n_images = n_images;
-  p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
-  const int tile_m = pair ? nearest::Cfg<true>::TILE_M : nearest::Cfg<false>::TILE_M;
-  const int group_m = pair ? nearest::Cfg<true>::GROUP_M : nearest::Cfg<false>::GROUP_M;
+  p.n_images = (int)(rows / patches);
+  p.num_kb = (channels + kb - 1) / kb;
+  const int tile_m = pair ? Cfg<MODE, true>::TILE_M : Cfg<MODE, false>::TILE_M;
+  const int group_m = pair ? Cfg<MODE, true>::GROUP_M : Cfg<MODE, false>::GROUP_M;
   p.num_m = (int)((rows + tile_m - 1) / tile_m);
-  p.num_n = (int)((rows + nearest::BN - 1) / nearest::BN);
-  sym_part_range(rows, patches, n_images, p.num_m, p.num_n, tile_m, group_m, part, parts, &p.tile_begin,
+  p.num_n = (int)((rows + BN - 1) / BN);
+  sym_part_range(rows, patches, p.n_images, p.num_m, p.num_n, tile_m, group_m, part, parts, &p.tile_begin,
                  &p.tile_end);
   if (p.tile_end <= p.tile_begin) return MUSC_B200_OK;  // nothing to do for this part
-  MUSC_TRY(set_smem_attr());
+  MUSC_TRY(set_nearest_smem_attrs());
   const int sms = sm_count();
   const int ctas = max_ctas > 0 && max_ctas < sms ? max_ctas : sms;
   if (!pair) {
-    nearest::nearest_kernel<true, false><<<ctas, nearest::THREADS, nearest::smem_bytes<false>(), s>>>(
-        mah, mal, mbh, mbl, p);
-    return check_launch("nearest_kernel<symmetric>");
+    nearest_kernel<MODE, false><<<ctas, Cfg<MODE, false>::THREADS, smem_bytes<MODE, false>(), s>>>(mah, mal, mbh,
+                                                                                                   mbl, p);
+    return check_launch(MODE == SCREEN ? "nearest_kernel<screen>" : "nearest_kernel<symmetric>");
   }
   // One cluster of two CTAs per SM pair, as many as can be resident at once.
   cudaLaunchConfig_t cfg = {};
@@ -982,18 +456,59 @@ int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, i
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(nearest::THREADS);
-  cfg.dynamicSmemBytes = nearest::smem_bytes<true>();
+  cfg.blockDim = dim3(Cfg<MODE, true>::THREADS);
+  cfg.dynamicSmemBytes = smem_bytes<MODE, true>();
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  MUSC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, nearest::nearest_kernel<true, true>, &cfg));
+  MUSC_CUDA(cudaOccupancyMaxActiveClusters(&clusters, nearest_kernel<MODE, true>, &cfg));
   if (clusters <= 0) return fail(MUSC_B200_ERR_CUDA, "nearest_pool: no CTA pair fits on this device");
   clusters = std::min(clusters, std::max(1, ctas / 2));
   cfg.gridDim = dim3(2 * clusters);
-  MUSC_CUDA(cudaLaunchKernelEx(&cfg, nearest::nearest_kernel<true, true>, mah, mal, mbh, mbl, p));
-  return check_launch("nearest_kernel<symmetric, pair>");
+  MUSC_CUDA(cudaLaunchKernelEx(&cfg, nearest_kernel<MODE, true>, mah, mal, mbh, mbl, p));
+  return check_launch(MODE == SCREEN ? "nearest_kernel<screen, pair>" : "nearest_kernel<symmetric, pair>");
+}
+
+static size_t table_entries(long long rows, int patches, long long rows_per_block) {
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  return (size_t)blocks * (size_t)(rows / patches) * (size_t)rows_per_block;
+}
+
+int nearest_pool_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
+                        int part, int parts, long long rows_per_block, int max_ctas, float* nearest_sq,
+                        cudaStream_t s) {
+  const size_t table = table_entries(rows, patches, rows_per_block);
+  MUSC_TRY(fill_table(nearest_sq, (long long)table, s));
+  // The scheduler counter lives in the 256 bytes after the table (musc_b200_nearest_pool_bytes).
+  unsigned long long* sched = reinterpret_cast<unsigned long long*>(
+      reinterpret_cast<uint8_t*>(nearest_sq) + (table * sizeof(float) + 255) / 256 * 256);
+  MUSC_CUDA(cudaMemsetAsync(sched, 0, sizeof(unsigned long long), s));
+  nearest::Params p{};
+  p.nearest = reinterpret_cast<unsigned int*>(nearest_sq);
+  p.sched = sched;
+  p.rows_per_block = rows_per_block;
+  p.blocked = rows_per_block < rows ? 1 : 0;
+  return pool_kernel_launch<nearest::SYM>(bank, bank_rows, rows, channels, patches, part, parts, max_ctas, p, s);
+}
+
+// Screen tables: k1 [blocks][N][rpb] uint64 and m2 (same shape, uint32), filled with
+// 0xFF bytes first ("unset", above every value); the scheduler word is zeroed.
+int screen_pool_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
+                       int part, int parts, long long rows_per_block, int max_ctas, unsigned long long* k1,
+                       unsigned int* m2, unsigned long long* sched, cudaStream_t s) {
+  const size_t n = table_entries(rows, patches, rows_per_block);
+  MUSC_CUDA(cudaMemsetAsync(k1, 0xFF, n * sizeof(unsigned long long), s));
+  MUSC_CUDA(cudaMemsetAsync(m2, 0xFF, n * sizeof(unsigned int), s));
+  MUSC_CUDA(cudaMemsetAsync(sched, 0, sizeof(unsigned long long), s));
+  nearest::Params p{};
+  p.k1 = k1;
+  p.m2 = m2;
+  p.sched = sched;
+  p.rows_per_block = rows_per_block;
+  p.blocked = rows_per_block < rows ? 1 : 0;
+  return pool_kernel_launch<nearest::SCREEN>(bank, bank_rows, rows, channels, patches, part, parts, max_ctas, p,
+                                             s);
 }
 
 int trimmed_launch(const float* nearest_sq, long long query_rows, int n_images, int rank_lo, int rank_hi,
@@ -1035,7 +550,7 @@ extern "C" int musc_b200_prep_bank(const float* z, long long rows, int channels,
   const long long blocks = (rows + kPrepWarps - 1) / kPrepWarps;
   prep_bank_kernel<<<(unsigned)blocks, kPrepWarps * 32, 0, s>>>(
       z, rows, channels, reinterpret_cast<__half*>(b + l.hi), reinterpret_cast<__half*>(b + l.lo),
-      reinterpret_cast<float*>(b + l.norm), reinterpret_cast<float*>(b + l.inv));
+      reinterpret_cast<float*>(b + l.norm), reinterpret_cast<float*>(b + l.inv), reinterpret_cast<float*>(b + l.lnorm));
   return check_launch("prep_bank_kernel");
 }
 
@@ -1074,6 +589,7 @@ extern "C" int musc_b200_bank_layout(long long rows, int channels, size_t* plane
   plane_offsets[1] = l.lo;
   plane_offsets[2] = l.norm;
   plane_offsets[3] = l.inv;
+  plane_offsets[4] = l.lnorm;
   return MUSC_B200_OK;
 }
 
@@ -1111,10 +627,111 @@ extern "C" int musc_b200_trimmed_mean(const float* nearest_sq, long long query_r
                         reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int musc_b200_screen_pool(const void* bank, long long bank_rows, long long rows, int channels,
+                                     int patches_per_image, int part, int n_parts, long long rows_per_block,
+                                     int max_ctas, void* k1, void* m2, void* sched_word, musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(rows, channels));
+  if (bank_rows < rows) return fail(MUSC_B200_ERR_INVALID, "screen_pool: bank_rows must be >= rows");
+  if (!bank || !k1 || !m2 || !sched_word) return fail(MUSC_B200_ERR_INVALID, "screen_pool: null pointer");
+  if (reinterpret_cast<uintptr_t>(bank) % 1024 != 0 || reinterpret_cast<uintptr_t>(k1) % 8 != 0 ||
+      reinterpret_cast<uintptr_t>(m2) % 4 != 0 || reinterpret_cast<uintptr_t>(sched_word) % 8 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "screen_pool: bank must be 1024-byte aligned, k1 and the word 8-byte, m2 4-byte");
+  if (patches_per_image <= 0 || rows % patches_per_image != 0 || rows / patches_per_image < 2)
+    return fail(MUSC_B200_ERR_INVALID, "screen_pool: rows must hold N >= 2 whole images");
+  if (patches_per_image > (1 << 24))
+    return fail(MUSC_B200_ERR_INVALID, "screen_pool: patches_per_image must be below 2^24");
+  if (n_parts <= 0 || part < 0 || part >= n_parts)
+    return fail(MUSC_B200_ERR_INVALID, "screen_pool: requires 0 <= part < n_parts");
+  if (rows_per_block <= 0 || rows_per_block % patches_per_image != 0)
+    return fail(MUSC_B200_ERR_INVALID, "screen_pool: rows_per_block must be a positive multiple of P");
+  MUSC_TRY(require_sm100());
+  return screen_pool_launch(bank, bank_rows, rows, channels, patches_per_image, part, n_parts, rows_per_block,
+                            max_ctas, static_cast<unsigned long long*>(k1), static_cast<unsigned int*>(m2),
+                            static_cast<unsigned long long*>(sched_word), reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t musc_b200_refine_bytes(int n_images, long long query_rows, int channels) {
+  if (n_images <= 0 || query_rows <= 0 || channels <= 0) return 0;
+  return refine_workspace_bytes(n_images, query_rows, channels);
+}
+
+extern "C" int musc_b200_refine(const void* bank, long long bank_rows, long long rows, int channels,
+                                int patches_per_image, long long first_row, long long query_rows, int rank_hi,
+                                const void* k1, const void* m2, int n_partials, long long partial_stride,
+                                long long table_rows, float* exact_sq, void* workspace, size_t workspace_bytes,
+                                musc_b200_stream stream) {
+  MUSC_TRY(check_bank_args(rows, channels));
+  if (!bank || !k1 || !m2 || !exact_sq || !workspace) return fail(MUSC_B200_ERR_INVALID, "refine: null pointer");
+  if (bank_rows < rows) return fail(MUSC_B200_ERR_INVALID, "refine: bank_rows must be >= rows");
+  if (reinterpret_cast<uintptr_t>(bank) % 1024 != 0 || reinterpret_cast<uintptr_t>(workspace) % 1024 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "refine: bank and workspace must be 1024-byte aligned");
+  if (reinterpret_cast<uintptr_t>(k1) % 8 != 0 || reinterpret_cast<uintptr_t>(m2) % 4 != 0 ||
+      reinterpret_cast<uintptr_t>(exact_sq) % 4 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "refine: misaligned table");
+  if (patches_per_image <= 0 || rows % patches_per_image != 0 || rows / patches_per_image < 2)
+    return fail(MUSC_B200_ERR_INVALID, "refine: rows must hold N >= 2 whole images");
+  const int n_images = (int)(rows / patches_per_image);
+  if (!(rank_hi >= 1 && rank_hi <= n_images - 1))
+    return fail(MUSC_B200_ERR_INVALID, "refine: requires 1 <= rank_hi <= N-1");
+  if (query_rows <= 0 || first_row < 0 || first_row + query_rows > rows || table_rows < query_rows)
+    return fail(MUSC_B200_ERR_INVALID, "refine: query rows must lie in the pool and in the tables");
+  if (n_partials <= 0 || (n_partials > 1 && partial_stride < (long long)n_images * table_rows))
+    return fail(MUSC_B200_ERR_INVALID, "refine: partial tables overlap");
+  if (workspace_bytes < refine_workspace_bytes(n_images, query_rows, channels))
+    return fail(MUSC_B200_ERR_WORKSPACE, "refine: workspace smaller than musc_b200_refine_bytes");
+  MUSC_TRY(require_sm100());
+  return refine_launch(bank, bank_rows, rows, channels, patches_per_image, first_row, query_rows, rank_hi,
+                       static_cast<const unsigned long long*>(k1), static_cast<const unsigned int*>(m2), n_partials,
+                       partial_stride, table_rows, exact_sq, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// MUSC_B200_MSM_EXACT=1 in the environment selects the 3-pass symmetric kernel for every
+// bank instead of the screen + refinement (same results within fp32 rounding).
+static bool use_exact_pool() {
+  const char* e = std::getenv("MUSC_B200_MSM_EXACT");
+  return e && e[0] == '1';
+}
+
+// Scratch of one bank's MSM after the bank itself: the exact path's table, or the screen
+// tables, the exact table and the refinement's workspace.
+static size_t msm_scratch_bytes(int n, int p, int c) {
+  const long long rows = (long long)n * p;
+  const size_t exact_path = align_up(musc_b200_nearest_pool_bytes(rows, p, rows), 1024);
+  const size_t entries = (size_t)n * rows;
+  const size_t deferred = align_up(entries * 8, 1024) + align_up(entries * 4, 1024) + 1024 +
+                          align_up(entries * sizeof(float), 1024) + align_up(refine_workspace_bytes(n, rows, c), 1024);
+  return std::max(exact_path, deferred);
+}
+
+// One prepared bank -> scores (the whole pool is one part).
+int msm_bank(const void* bank, int n, int p, int c, int rank_lo, int rank_hi, double* scores, void* scratch,
+             cudaStream_t s) {
+  const long long rows = (long long)n * p;
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  musc_b200_stream st = reinterpret_cast<musc_b200_stream>(s);
+  if (use_exact_pool()) {
+    float* table = reinterpret_cast<float*>(ws);
+    MUSC_TRY(musc_b200_nearest_pool(bank, rows, rows, c, p, 0, 1, rows, 0, table, st));
+    return musc_b200_trimmed_mean(table, rows, n, rank_lo, rank_hi, scores, st);
+  }
+  const size_t entries = (size_t)n * rows;
+  uint8_t* k1 = ws;
+  uint8_t* m2 = k1 + align_up(entries * 8, 1024);
+  uint8_t* word = m2 + align_up(entries * 4, 1024);
+  float* exact = reinterpret_cast<float*>(word + 1024);
+  uint8_t* rws = word + 1024 + align_up(entries * sizeof(float), 1024);
+  MUSC_TRY(musc_b200_screen_pool(bank, rows, rows, c, p, 0, 1, rows, 0, k1, m2, word, st));
+  MUSC_TRY(musc_b200_refine(bank, rows, rows, c, p, 0, rows, rank_hi, k1, m2, 1, 0, rows, exact, rws,
+                            refine_workspace_bytes(n, rows, c), st));
+  return musc_b200_trimmed_mean(exact, rows, n, rank_lo, rank_hi, scores, st);
+}
+
+size_t msm_bank_scratch_bytes(int n, int p, int c) { return msm_scratch_bytes(n, p, c); }
+
 extern "C" size_t musc_b200_msm_workspace_bytes(int n, int p, int c) {
   if (n <= 0 || p <= 0 || c <= 0) return 0;
   const long long rows = (long long)n * p;
-  return bank_layout(rows, c).total + align_up(musc_b200_nearest_pool_bytes(rows, p, rows), 1024);
+  return bank_layout(rows, c).total + msm_scratch_bytes(n, p, c);
 }
 
 extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi, double* scores,
@@ -1131,8 +748,6 @@ extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, i
     return fail(MUSC_B200_ERR_INVALID, "msm: workspace must be 1024-byte aligned");
   const size_t bank_size = bank_layout(rows, c).total;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* table = reinterpret_cast<float*>(ws + bank_size);
   MUSC_TRY(musc_b200_prep_bank(z, rows, c, ws, bank_size, stream));
-  MUSC_TRY(musc_b200_nearest_pool(ws, rows, rows, c, p, 0, 1, rows, 0, table, stream));
-  return musc_b200_trimmed_mean(table, rows, n, rank_lo, rank_hi, scores, stream);
+  return msm_bank(ws, n, p, c, rank_lo, rank_hi, scores, ws + bank_size, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -9,6 +9,11 @@
 
 #include <algorithm>
 
+// Implemented in msm.cu: one prepared bank -> scores, and its scratch size.
+int msm_bank(const void* bank, int n, int p, int c, int rank_lo, int rank_hi, double* scores, void* scratch,
+             cudaStream_t s);
+size_t msm_bank_scratch_bytes(int n, int p, int c);
+
 namespace musc {
 namespace {
 
@@ -25,7 +30,7 @@ PoolWorkspace pool_layout(int n, int p, int c, int n_radii) {
   w.z = align_1k(musc_b200_lnamd_workspace_bytes(n));
   w.bank = w.z + align_1k((size_t)n_radii * rows * c * sizeof(float));
   w.table = w.bank + align_1k(musc_b200_bank_bytes(rows, c));
-  w.total = w.table + align_1k(musc_b200_nearest_pool_bytes(rows, p, rows));
+  w.total = w.table + align_1k(msm_bank_scratch_bytes(n, p, c));
   return w;
 }
 
@@ -72,7 +77,6 @@ extern "C" int musc_b200_score_pool(const void* const* tokens, int dtype, int n_
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const long long rows = (long long)n_images * p;
   float* z = reinterpret_cast<float*>(ws + w.z);
-  float* table = reinterpret_cast<float*>(ws + w.table);
   for (int li = 0; li < n_layers; ++li) {
     float* outs[3];
     for (int ri = 0; ri < n_radii; ++ri) outs[ri] = z + (size_t)ri * rows * channels;
@@ -80,9 +84,8 @@ extern "C" int musc_b200_score_pool(const void* const* tokens, int dtype, int n_
                              (long long)p * channels, channels, 1, ws + w.stats, w.z - w.stats, stream));
     for (int ri = 0; ri < n_radii; ++ri) {
       MUSC_TRY(musc_b200_prep_bank(outs[ri], rows, channels, ws + w.bank, w.table - w.bank, stream));
-      MUSC_TRY(musc_b200_nearest_pool(ws + w.bank, rows, rows, channels, p, 0, 1, rows, 0, table, stream));
-      MUSC_TRY(musc_b200_trimmed_mean(table, rows, n_images, a, b,
-                                      scores + ((size_t)ri * n_layers + li) * rows, stream));
+      MUSC_TRY(msm_bank(ws + w.bank, n_images, p, channels, a, b, scores + ((size_t)ri * n_layers + li) * rows,
+                        ws + w.table, reinterpret_cast<cudaStream_t>(stream)));
     }
   }
   return musc_b200_score_maps(scores, n_radii, n_layers, n_images, side, image_size, maps, image_max, nullptr,

@@ -39,6 +39,10 @@ SIGNATURES = {
     'musc_b200_nearest_pool_bytes': (_sz, [_ll, _int, _ll]),
     'musc_b200_nearest_pool': (_int, [_vp, _ll, _ll, _int, _int, _int, _int, _ll, _int, _vp, _vp]),
     'musc_b200_bank_layout': (_int, [_ll, _int, ctypes.POINTER(_sz)]),
+    'musc_b200_screen_pool': (_int, [_vp, _ll, _ll, _int, _int, _int, _int, _ll, _int, _vp, _vp, _vp, _vp]),
+    'musc_b200_refine_bytes': (_sz, [_int, _ll, _int]),
+    'musc_b200_refine': (_int, [_vp, _ll, _ll, _int, _int, _ll, _ll, _int, _vp, _vp, _int, _ll, _ll, _vp, _vp,
+                                _sz, _vp]),
     'musc_b200_trimmed_mean': (_int, [_vp, _ll, _int, _int, _int, _vp, _vp]),
     'musc_b200_msm_workspace_bytes': (_sz, [_int, _int, _int]),
     'musc_b200_msm': (_int, [_vp, _int, _int, _int, _int, _int, _vp, _vp, _sz, _vp]),

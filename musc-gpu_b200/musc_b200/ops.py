@@ -206,13 +206,77 @@ def empty_bank(rows: int, channels: int, device) -> torch.Tensor:
 
 
 def bank_planes(bank: torch.Tensor, rows: int, channels: int, layout_rows: int | None = None):
-    """uint8 views of the first ``rows`` rows of each plane (hi, lo, |z|^2, 2^-k) of a bank
-    laid out for ``layout_rows`` rows -- the pieces a rank contributes to a gathered bank."""
+    """uint8 views of the first ``rows`` rows of each plane (hi, lo, |z|^2, 2^-k, residual
+    norm) of a bank laid out for ``layout_rows`` rows -- the pieces a rank contributes to a
+    gathered bank."""
     layout_rows = rows if layout_rows is None else layout_rows
-    offs = (ctypes.c_size_t * 4)()
+    offs = (ctypes.c_size_t * 5)()
     _lib.check(_lib.lib().musc_b200_bank_layout(layout_rows, channels, offs), 'musc_b200_bank_layout')
-    sizes = (rows * channels * 2, rows * channels * 2, rows * 4, rows * 4)
+    sizes = (rows * channels * 2, rows * channels * 2, rows * 4, rows * 4, rows * 4)
     return [bank[o:o + n] for o, n in zip(offs, sizes)]
+
+
+def screen_table(rows: int, patches: int, rows_per_block: int | None = None, device=None,
+                 min_blocks: int = 1) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Uninitialised screen tables for :func:`screen_pool`: ``(k1, m2, word)`` with
+    ``k1`` ``(blocks, n_images, rpb)`` int64 and ``m2`` the same shape int32 (the signed
+    types hold the unsigned keys bit for bit) and ``word`` the scheduler's int64.
+    ``min_blocks`` pads the block count (an all-to-all over more ranks than blocks; the
+    padding is never filled)."""
+    rpb = rows if rows_per_block is None else rows_per_block
+    n_images = rows // patches
+    blocks = max(-(-rows // rpb), min_blocks)
+    dev = torch.device(device) if device is not None else None
+    k1 = torch.empty(blocks, n_images, rpb, dtype=torch.int64, device=dev)
+    m2 = torch.empty(blocks, n_images, rpb, dtype=torch.int32, device=dev)
+    word = torch.empty(1, dtype=torch.int64, device=dev)
+    return k1, m2, word
+
+
+def screen_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part: int = 0, parts: int = 1,
+                rows_per_block: int | None = None, out=None, bank_rows: int | None = None,
+                max_ctas: int = 0):
+    """Screened symmetric pool pass (one fp16 MMA pass): ``(k1, m2, word)`` of :func:`screen_table`."""
+    dev = bank.device
+    rpb = rows if rows_per_block is None else rows_per_block
+    if out is None:
+        out = screen_table(rows, patches, rpb, dev)
+    k1, m2, word = out
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_screen_pool(_ptr(bank), rows if bank_rows is None else bank_rows, rows,
+                                              channels, patches, part, parts, rpb, int(max_ctas), _ptr(k1),
+                                              _ptr(m2), _ptr(word), _stream(dev))
+        _lib.check(st, 'musc_b200_screen_pool')
+    return out
+
+
+def refine(bank: torch.Tensor, rows: int, channels: int, patches: int, first_row: int, query_rows: int,
+           rank_hi: int, k1: torch.Tensor, m2: torch.Tensor, out: torch.Tensor | None = None,
+           bank_rows: int | None = None) -> torch.Tensor:
+    """Exact squared minima ``(n_images, query_rows)`` float32 from screen tables.
+
+    ``k1`` / ``m2``: ``(parts, n_images, table_rows)`` partial screen tables covering the
+    query rows (local row = row - first_row), one per part of the pool's tile list.
+    Images that cannot reach the trimmed ranks ``[.., rank_hi)`` hold FLT_MAX.
+    """
+    dev = bank.device
+    n_images = rows // patches
+    if k1.ndim == 2:
+        k1, m2 = k1.unsqueeze(0), m2.unsqueeze(0)
+    parts, _, table_rows = k1.shape
+    if not (k1.is_contiguous() and m2.is_contiguous()):
+        raise ValueError('refine: screen tables must be contiguous')
+    if out is None:
+        out = torch.empty(n_images, query_rows, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        ws_bytes = lib.musc_b200_refine_bytes(n_images, query_rows, channels)
+        ws = _aligned_empty(ws_bytes, dev)
+        st = lib.musc_b200_refine(_ptr(bank), rows if bank_rows is None else bank_rows, rows, channels, patches,
+                                  first_row, query_rows, rank_hi, _ptr(k1), _ptr(m2), parts, n_images * table_rows,
+                                  table_rows, _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(st, 'musc_b200_refine')
+    return out
 
 
 def nearest_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part: int = 0,

@@ -10,13 +10,19 @@ This is the scoring half of ``MuSc.make_category_data``
   distance/min GEMM and the interval average;
 * layer and radius means, up-sampling and image maxima (``:259-288``).
 
+Each bank's MSM is the screened symmetric pass (one fp16 MMA pass over every
+unordered pair of patches from different images) followed by the refinement
+to exact minima of the pairs that can reach the trimmed ranks (the reference
+GPU driver's rank-deferred scheme, ``models/modules/_MSM_gpu.py:739-786``);
+``MUSC_B200_MSM_EXACT=1`` selects the 3-pass exact kernel for every pair.
+
 Multi-GPU (one process per GPU): rank r owns the query images
 ``[r*ceil(N/G), ...)`` and aggregates only those; each bank is all-gathered
-over NCCL (overlapped with the previous bank's work), every rank evaluates a
-balanced share of the pool's symmetric distance tiles, and a MIN
-reduce-scatter of the nearest table gives each rank the minima of its own
-query rows.  The reference is single-device; the sharding is this library's
-addition.
+over NCCL (overlapped with the previous bank's work), every rank screens a
+balanced share of the pool's symmetric distance tiles into tables blocked by
+the rows' owners, and an all-to-all hands each rank the partial tables of its
+own query rows, which it refines.  The reference is single-device; the
+sharding is this library's addition.
 """
 from __future__ import annotations
 
@@ -71,7 +77,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     l's event just before that layer's LNAMD, so later layers' copies overlap
     the scoring of earlier ones.  Banks are processed layer by layer.
     ``collective_sms``: with a process group, SMs left free during each bank's
-    GEMM so the neighbouring banks' gather and reduce-scatter run alongside it
+    GEMM so the neighbouring banks' gather and exchange run alongside it
     (0 = none, the default: the GEMM's dynamic tile scheduler already lets a
     collective that starts first keep its SMs).
     ``verify``: with a process group, re-score the last bank on every rank as one
@@ -126,11 +132,11 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
 
     # 2. Per bank: prep, (gather), symmetric nearest minima, interval average.
     #    One GPU: prep the whole bank, one symmetric launch, select.
-    #    G GPUs: each rank preps the bank of its own rows; the four bank planes are
+    #    G GPUs: each rank preps the bank of its own rows; the five bank planes are
     #    all-gathered into a padded pool bank (the next bank's gather overlaps this
-    #    bank's GEMM); rank r evaluates part r of the symmetric tile list into a table
-    #    whose blocks are the ranks' query rows; a MIN reduce-scatter (overlapping the
-    #    next bank's GEMM) hands each rank the minima of its own rows.
+    #    bank's GEMM); rank r screens part r of the symmetric tile list into tables
+    #    whose blocks are the ranks' query rows; an all-to-all (overlapping the next
+    #    bank's GEMM) hands each rank the partial tables of its own rows to refine.
     banks = [(li, ri) for li in range(n_l) for ri in range(n_r)]
     verified = None
     scores = torch.empty(n_r, n_l, n_local, p, dtype=torch.float64, device=dev)
@@ -139,64 +145,111 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     rpb = per * p if world > 1 else rows
 
     def select(near: torch.Tensor, li: int, ri: int) -> None:
+        # near: (N, width) table whose first q_rows columns are this rank's rows
         if q_rows == 0:
             return
-        if q_rows == rpb:
+        if near.shape[1] == q_rows:
             kernels.trimmed_mean(near, a, b, out=scores[ri, li].view(-1))
         else:
-            tmp = torch.empty(rpb, dtype=torch.float64, device=dev)
+            tmp = torch.empty(near.shape[1], dtype=torch.float64, device=dev)
             kernels.trimmed_mean(near, a, b, out=tmp)
             scores[ri, li].view(-1).copy_(tmp[:q_rows])
 
+    exact_path = exact_pool_path()
     if world == 1:
-        table = kernels.nearest_pool_table(rows, p, rows, dev)
         bank = kernels.empty_bank(rows, c, dev)
+        if exact_path:
+            table = kernels.nearest_pool_table(rows, p, rows, dev)
+        else:
+            screen = kernels.screen_table(rows, p, rows, dev)
+            table = torch.empty(1, n_images, rows, dtype=torch.float32, device=dev)
         for li, ri in banks:
             aggregate(li)
             kernels.prep_bank(local[li, ri, :n_images].reshape(rows, c), out=bank)
-            kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, out=table)
+            if exact_path:
+                kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, out=table)
+            else:
+                kernels.screen_pool(bank, rows, c, p, 0, 1, rows, out=screen)
+                kernels.refine(bank, rows, c, p, 0, rows, b, screen[0], screen[1], out=table[0])
             select(table[0], li, ri)
     else:
         local_rows, bank_rows = per * p, world * per * p
         sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
         max_ctas = max(1, sms - collective_sms) if (sms and collective_sms) else 0
         # The gathers run on their own communicator (own NCCL stream), so bank k+1's gather
-        # is never queued behind bank k-1's reduce-scatter, which must wait for GEMM k-1.
+        # is never queued behind bank k-1's exchange, which must wait for GEMM k-1.
         gather_group = _side_group(group)
         local_bank = [kernels.empty_bank(local_rows, c, dev) for _ in range(2)]
-        full_bank = [kernels.empty_bank(bank_rows, c, dev) for _ in range(2)]
-        tables = [kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world) for _ in range(3)]
-        mine = [torch.empty(n_images, rpb, dtype=torch.float32, device=dev) for _ in range(3)]
+        full_bank = [kernels.empty_bank(bank_rows, c, dev) for _ in range(3)]
 
         def start_gather(k):
             li, ri = banks[k]
             aggregate(li)
             kernels.prep_bank(local[li, ri].reshape(local_rows, c), out=local_bank[k % 2])
-            pieces = zip(kernels.bank_planes(full_bank[k % 2], bank_rows, c),
+            pieces = zip(kernels.bank_planes(full_bank[k % 3], bank_rows, c),
                          kernels.bank_planes(local_bank[k % 2], local_rows, c))
             return [dist.all_gather_into_tensor(f, l, group=gather_group, async_op=True) for f, l in pieces]
 
+        if exact_path:
+            tables = [kernels.nearest_pool_table(rows, p, rpb, dev, min_blocks=world) for _ in range(3)]
+            mine = [torch.empty(n_images, rpb, dtype=torch.float32, device=dev) for _ in range(3)]
+        else:
+            # Each rank screens part r of the symmetric tiles into tables blocked by the
+            # rows' owners; an all-to-all hands every rank the partial tables of its own
+            # rows, which the refinement combines (not a plain minimum: the second minimum
+            # also takes the partial minima that lose).
+            screens = [kernels.screen_table(rows, p, rpb, dev, min_blocks=world) for _ in range(2)]
+            recv = [(torch.empty(world, n_images, rpb, dtype=torch.int64, device=dev),
+                     torch.empty(world, n_images, rpb, dtype=torch.int32, device=dev)) for _ in range(2)]
+            exact_t = torch.empty(n_images, max(q_rows, 1), dtype=torch.float32, device=dev)
+
+            def start_exchange(k):
+                k1, m2, _ = screens[k % 2]
+                rk, rm = recv[k % 2]
+                return [dist.all_to_all_single(rk, k1[:world], group=group, async_op=True),
+                        dist.all_to_all_single(rm, m2[:world], group=group, async_op=True)]
+
+            def finish_bank(k, works):
+                for w in works:
+                    w.wait()
+                if q_rows:
+                    rk, rm = recv[k % 2]
+                    kernels.refine(full_bank[k % 3], rows, c, p, first * p, q_rows, b, rk, rm, out=exact_t,
+                                   bank_rows=bank_rows)
+                    select(exact_t, *banks[k])
+
         gathers = {0: start_gather(0)}
-        pending = []   # (finish_reduce_scatter, k), completed two banks later
+        pending = []   # (finish, k): reduce-scatter or exchange in flight
         for k, (li, ri) in enumerate(banks):
             if k + 1 < len(banks):
                 gathers[k + 1] = start_gather(k + 1)
             for w in gathers.pop(k):
                 w.wait()
-            kernels.nearest_pool(full_bank[k % 2], rows, c, p, rank, world, rpb, out=tables[k % 3],
-                                 bank_rows=bank_rows, max_ctas=max_ctas)
-            pending.append((_min_reduce_scatter(tables[k % 3], mine[k % 3], rank, group), k))
-            if len(pending) > 2:
-                finish, kk = pending.pop(0)
-                finish()
+            if exact_path:
+                kernels.nearest_pool(full_bank[k % 3], rows, c, p, rank, world, rpb, out=tables[k % 3],
+                                     bank_rows=bank_rows, max_ctas=max_ctas)
+                pending.append((_min_reduce_scatter(tables[k % 3], mine[k % 3], rank, group), k))
+                if len(pending) > 2:
+                    finish, kk = pending.pop(0)
+                    finish()
+                    select(mine[kk % 3], *banks[kk])
+            else:
+                kernels.screen_pool(full_bank[k % 3], rows, c, p, rank, world, rpb, out=screens[k % 2],
+                                    bank_rows=bank_rows, max_ctas=max_ctas)
+                pending.append((start_exchange(k), k))
+                if len(pending) > 1:
+                    works, kk = pending.pop(0)
+                    finish_bank(kk, works)
+        for item, kk in pending:
+            if exact_path:
+                item()
                 select(mine[kk % 3], *banks[kk])
-        for finish, kk in pending:
-            finish()
-            select(mine[kk % 3], *banks[kk])
+            else:
+                finish_bank(kk, item)
         if verify:
-            verified = _verify_last_bank(kernels, full_bank[(len(banks) - 1) % 2], bank_rows, rows, c, p,
+            verified = _verify_last_bank(kernels, full_bank[(len(banks) - 1) % 3], bank_rows, rows, c, p,
                                          n_images, first, q_rows, a, b, scores[banks[-1][1], banks[-1][0]],
-                                         banks[-1], group)
+                                         banks[-1], group, exact_path)
 
     # 3. Layer/radius means, up-sampling, image maxima for the local images.
     if n_local:
@@ -207,15 +260,22 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     return PoolScores(scores, maps, image_max, first, n_images, verified)
 
 
-def _verify_last_bank(kernels, bank, bank_rows, rows, c, p, n_images, first, q_rows, a, b, got, bank_id, group):
+def _verify_last_bank(kernels, bank, bank_rows, rows, c, p, n_images, first, q_rows, a, b, got, bank_id, group,
+                      exact_path):
     """Every rank scores the gathered bank as one part (the single-GPU computation) and
     compares its own query rows with the sharded scores ``got``; counts summed over ranks."""
     import torch.distributed as dist
     dev = got.device
-    whole = kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, bank_rows=bank_rows)[0]   # (N, rows)
     mism = torch.zeros(3, dtype=torch.float64, device=dev)
     if q_rows:
-        mine = whole[:, first * p:first * p + q_rows].contiguous()
+        if exact_path:
+            whole = kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, bank_rows=bank_rows)[0]   # (N, rows)
+            mine = whole[:, first * p:first * p + q_rows].contiguous()
+        else:
+            k1, m2, _ = kernels.screen_pool(bank, rows, c, p, 0, 1, rows, bank_rows=bank_rows)
+            k1 = k1[:, :, first * p:first * p + q_rows].contiguous()
+            m2 = m2[:, :, first * p:first * p + q_rows].contiguous()
+            mine = kernels.refine(bank, rows, c, p, first * p, q_rows, b, k1, m2, bank_rows=bank_rows)
         ref = kernels.trimmed_mean(mine, a, b)
         sharded = got.reshape(-1)
         diff = (ref - sharded).abs()
@@ -228,6 +288,13 @@ def _verify_last_bank(kernels, bank, bank_rows, rows, c, p, n_images, first, q_r
     bad, worst, checked = mism.tolist()
     return {'bank': {'layer': bank_id[0], 'radius_index': bank_id[1]}, 'rows_checked': int(checked),
             'rows_differing': int(bad), 'max_abs_diff': worst, 'bit_exact': bad == 0}
+
+
+def exact_pool_path() -> bool:
+    """``MUSC_B200_MSM_EXACT=1``: score every bank with the 3-pass exact kernel instead of the
+    screen + refinement (the same switch as the C library's ``musc_b200_msm``)."""
+    import os
+    return os.environ.get('MUSC_B200_MSM_EXACT', '0') == '1'
 
 
 _SIDE_GROUPS: dict = {}

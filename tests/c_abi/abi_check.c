@@ -18,7 +18,7 @@ static void expect(int cond, const char* what) {
 }
 
 int main(void) {
-  expect(musc_b200_abi_version() == 1, "abi version");
+  expect(musc_b200_abi_version() == 2, "abi version");
   expect(musc_b200_lnamd_workspace_bytes(4) == 4 * 8 * 2 * sizeof(double), "lnamd workspace");
   expect(musc_b200_bank_bytes(1369, 1024) % 1024 == 0, "bank bytes aligned");
   expect(musc_b200_nearest_pool_bytes(16 * 1369, 1369, 16 * 1369) >= (size_t)16 * 16 * 1369 * 4,
@@ -27,10 +27,26 @@ int main(void) {
          "score pool workspace");
   expect(musc_b200_score_pool_bytes(0, 1370, 1024, 3) == 0, "score pool workspace, no images");
 
-  size_t planes[4];
+  size_t planes[5];
   expect(musc_b200_bank_layout(1369, 1024, planes) == MUSC_B200_OK, "bank layout");
-  expect(planes[0] == 0 && planes[1] > planes[0] && planes[2] > planes[1] && planes[3] > planes[2],
+  expect(planes[0] == 0 && planes[1] > planes[0] && planes[2] > planes[1] && planes[3] > planes[2] &&
+             planes[4] > planes[3] && musc_b200_bank_bytes(1369, 1024) > planes[4],
          "bank planes ordered");
+  expect(musc_b200_refine_bytes(16, 16 * 1369, 1024) > (size_t)16 * 16 * 1369 * 4, "refine workspace");
+  expect(musc_b200_refine_bytes(0, 16 * 1369, 1024) == 0, "refine workspace, no images");
+
+  /* screen and refinement contract violations */
+  expect(musc_b200_screen_pool((const void*)(size_t)1024, 2738, 2738, 64, 1369, 0, 1, 2738, 0, NULL,
+                               (void*)(size_t)1024, (void*)(size_t)1024, NULL) == MUSC_B200_ERR_INVALID,
+         "screen null table");
+  expect(musc_b200_screen_pool((const void*)(size_t)1024, 2738, 2738, 64, 1369, 2, 2, 2738, 0,
+                               (void*)(size_t)1024, (void*)(size_t)1024, (void*)(size_t)1024, NULL) ==
+             MUSC_B200_ERR_INVALID,
+         "screen part out of range");
+  expect(musc_b200_refine((const void*)(size_t)1024, 2738, 2738, 64, 1369, 0, 2738, 2,
+                          (const void*)(size_t)1024, (const void*)(size_t)1024, 1, 0, 2738,
+                          (float*)(size_t)1024, (void*)(size_t)1024, (size_t)1 << 40, NULL) == MUSC_B200_ERR_INVALID,
+         "refine rank beyond N-1");
 
   /* contract violations: reported before any CUDA call */
   expect(musc_b200_trimmed_mean(NULL, 10, 5, 0, 1, NULL, NULL) == MUSC_B200_ERR_INVALID, "trimmed null");

@@ -80,6 +80,63 @@ class OracleKernels:
         return out
 
     @staticmethod
+    def screen_table(rows, patches, rpb, device, min_blocks=1):
+        blocks = max(-(-rows // rpb), min_blocks)
+        n = rows // patches
+        return (torch.empty(blocks, n, rpb, dtype=torch.int64), torch.empty(blocks, n, rpb, dtype=torch.int32),
+                torch.empty(1, dtype=torch.int64))
+
+    @staticmethod
+    def screen_pool(bank, rows, c, p, part, parts, rpb, out=None, bank_rows=None, max_ctas=0):
+        """The screen tables' contract for the pairs {i, j} with min(i, j) % parts == part:
+        k1 = (bits of the smallest squared distance with the low 8 bits cleared) << 32 | patch,
+        m2 = bits of the second smallest (low 8 bits cleared); -1 (all ones) where unset."""
+        n = rows // p
+        if out is None:
+            out = OracleKernels.screen_table(rows, p, rpb, None)
+        k1, m2, _ = out
+        k1.fill_(-1)
+        m2.fill_(-1)
+        z = bank[:rows].numpy().reshape(n, p, c).astype(np.float64)
+        for i in range(n):
+            for j in range(n):
+                if i == j or min(i, j) % parts != part:
+                    continue
+                d2 = ((z[i][:, None, :] - z[j][None, :, :]) ** 2).sum(-1).astype(np.float32)  # rows of i vs j
+                bits = (d2.view(np.uint32) & np.uint32(0xFFFFFF00)).astype(np.int64)
+                order = np.argsort(bits, axis=1, kind='stable')
+                for q in range(p):
+                    row = i * p + q
+                    best, second = order[q, 0], order[q, 1] if p > 1 else None
+                    key = (int(bits[q, best]) << 32) | int(best)
+                    k1[row // rpb, j, row % rpb] = key - (1 << 64) if key >= (1 << 63) else key
+                    if second is not None:
+                        m2[row // rpb, j, row % rpb] = int(np.int64(bits[q, second]).astype(np.uint32).view(np.int32))
+        return out
+
+    @staticmethod
+    def refine(bank, rows, c, p, first_row, q_rows, rank_hi, k1, m2, out=None, bank_rows=None):
+        """Exact minima of the query rows (float32 identity as the oracle's nearest table),
+        after checking that the partial screen tables combine to the exact argmin."""
+        n = rows // p
+        z = bank[:rows].numpy().reshape(n * p, c).astype(np.float64)
+        if out is None:
+            out = torch.empty(n, q_rows, dtype=torch.float32)
+        k1u = k1.numpy().view(np.uint64)
+        for q in range(q_rows):
+            g = first_row + q
+            img = g // p
+            for j in range(n):
+                if j == img:
+                    out[j, q] = float(np.finfo(np.float32).max)
+                    continue
+                d2 = ((z[j * p:(j + 1) * p] - z[g]) ** 2).sum(-1)
+                best = int(k1u[:, j, q].min() & np.uint64(0xFFFFFFFF))
+                assert abs(d2[best] - d2.min()) <= 1e-6 * max(d2.min(), 1e-12) + 1e-12, 'combined argmin'
+                out[j, q] = float(np.float32(d2.min()))
+        return out
+
+    @staticmethod
     def trimmed_mean(near, a, b, out=None):
         if out is None:
             out = torch.empty(near.shape[1], dtype=torch.float64)

@@ -389,3 +389,133 @@ def test_config3_super_fast_pool100_against_oracle(cuda_device):
         _, want_mx = oreduce.image_scores(want[None, None, None], 518)
         np.testing.assert_allclose(mx[i], want_mx[0], rtol=RTOL, atol=0)
     assert _lib_device_error_clear()
+
+
+# --------------------------------------------------------------------------- screen + refinement
+def _exact_tables(z: np.ndarray):
+    """float64 squared distances per (row, image): min, argmin and second min (self image skipped)."""
+    n, p, c = z.shape
+    flat = z.reshape(n * p, c).astype(np.float64)
+    d2 = ((flat[:, None, :] - flat[None, :, :]) ** 2).sum(-1).reshape(n * p, n, p)
+    order = np.argsort(d2, axis=2, kind='stable')
+    mins = np.take_along_axis(d2, order[:, :, :1], 2)[..., 0]
+    second = np.take_along_axis(d2, order[:, :, 1:2], 2)[..., 0] if p > 1 else np.full_like(mins, np.inf)
+    return mins, order[:, :, 0], second, d2
+
+
+@pytest.mark.parametrize('n,p,c', [(5, 49, 64), (7, 300, 128), (4, 1369, 64)])
+def test_screen_tables_bound_the_exact_minima(cuda_device, n, p, c):
+    """nearest_kernel<SCREEN>: the key's patch attains a distance within the screen's error
+    of the exact minimum, its value is that screened distance, and the second-smallest value
+    is a screened second minimum (within the bound of the exact second smallest)."""
+    from musc_b200 import ops
+    z = torch.randn(n, p, c, generator=torch.Generator().manual_seed(n * 31 + p))
+    z = z / z.norm(dim=-1, keepdim=True)
+    bank = ops.prep_bank(z.reshape(n * p, c).to(cuda_device))
+    k1, m2, _ = ops.screen_pool(bank, n * p, c, p)
+    k1 = k1[0].cpu().numpy().view(np.uint64).T            # (rows, n)
+    m2 = m2[0].cpu().numpy().view(np.uint32).T
+    mins, _, second, d2 = _exact_tables(z.numpy())
+    tol = 2.5e-3                                          # the screen's certified bound is ~1.1e-3 here
+    for row in range(n * p):
+        for j in range(n):
+            if j == row // p:
+                assert k1[row, j] == np.uint64(0xFFFFFFFFFFFFFFFF)
+                continue
+            patch = int(k1[row, j] & np.uint64(0xFFFFFFFF))
+            val = np.uint32(k1[row, j] >> np.uint64(32)).view(np.float32)
+            assert 0 <= patch < p
+            assert d2[row, j, patch] <= mins[row, j] + tol
+            assert abs(float(val) - d2[row, j, patch]) <= tol
+            assert float(np.uint32(m2[row, j]).view(np.float32)) >= second[row, j] - tol
+
+
+@pytest.mark.parametrize('n,p,c,dup', [(6, 49, 64, False), (9, 100, 32, True), (5, 300, 1024, False),
+                                       (11, 1369, 64, False), (8, 196, 64, True)])
+def test_refine_equals_exact_path(cuda_device, n, p, c, dup):
+    """screen + refinement vs the 3-pass exact table: every entry the refinement keeps is the
+    exact minimum, entries it drops lie above the rank threshold, and the interval averages
+    agree; with duplicated patches (exact ties, zero distances) most pairs go through the
+    gathered 3-pass fallback."""
+    from musc_b200 import ops
+    g = torch.Generator().manual_seed(n * 7 + c)
+    z = torch.randn(n, p, c, generator=g)
+    if dup:
+        z[:, 1::2] = z[:, 0::2][:, :z[:, 1::2].shape[1]]          # every other patch repeated
+        z[1] = z[0]                                              # and a duplicated image
+    z = z / z.norm(dim=-1, keepdim=True)
+    rows = n * p
+    bank = ops.prep_bank(z.reshape(rows, c).to(cuda_device))
+    exact = ops.nearest_pool(bank, rows, c, p)[0]
+    for lo, hi in [(0, max(1, int((n - 1) * 0.3))), (1, n - 1)]:
+        if hi <= lo:
+            continue
+        k1, m2, _ = ops.screen_pool(bank, rows, c, p)
+        ref = ops.refine(bank, rows, c, p, 0, rows, hi, k1, m2)
+        kept = ref != torch.finfo(torch.float32).max
+        torch.testing.assert_close(ref[kept], exact[kept], rtol=2e-5, atol=2e-6)
+        s_ref = ops.trimmed_mean(ref, lo, hi)
+        s_exact = ops.trimmed_mean(exact, lo, hi)
+        # zero distances: the 3-pass identity leaves sqrt(fp32 rounding noise), the exact fp32
+        # difference gives 0 (the duplicate-patch convention of the golden cases: 2e-3 absolute)
+        torch.testing.assert_close(s_ref, s_exact, rtol=2e-6, atol=2e-3 if dup else 2e-6)
+    assert _lib_device_error_clear()
+
+
+@pytest.mark.parametrize('parts', [2, 3])
+def test_refine_combines_partial_screens_exactly(cuda_device, parts):
+    """Per-rank screen parts, handed to the refinement as partial tables of the rows each
+    rank owns, give the single-part refinement bit for bit (the all-to-all path)."""
+    from musc_b200 import ops
+    from musc_b200.pipeline import shard_range
+    n, p, c = 10, 1369, 64
+    z = torch.randn(n * p, c, generator=torch.Generator().manual_seed(parts + 40)).to(cuda_device)
+    bank = ops.prep_bank(z)
+    rows = n * p
+    _, _, per = shard_range(n, parts, 0)
+    rpb = per * p
+    k1w, m2w, _ = ops.screen_pool(bank, rows, c, p)
+    b = int((n - 1) * 0.3)
+    whole = ops.refine(bank, rows, c, p, 0, rows, b, k1w, m2w)
+    tabs = [ops.screen_pool(bank, rows, c, p, k, parts, rpb, out=ops.screen_table(rows, p, rpb, cuda_device,
+                                                                                 min_blocks=parts))
+            for k in range(parts)]
+    for r in range(parts):
+        first, end, _ = shard_range(n, parts, r)
+        q_rows = (end - first) * p
+        if q_rows == 0:
+            continue
+        k1 = torch.stack([t[0][r] for t in tabs]).contiguous()
+        m2 = torch.stack([t[1][r] for t in tabs]).contiguous()
+        got = ops.refine(bank, rows, c, p, first * p, q_rows, b, k1, m2)
+        assert torch.equal(got, whole[:, first * p:first * p + q_rows])
+
+
+def test_refine_rescue_when_the_staging_bank_overflows(cuda_device):
+    """A pool of repeated patches (every pair a tie, nothing certifiable) with the interval
+    reaching every image queues more rows than the staging bank holds; the overflow goes
+    through the exact fp32 rescue and the scores still match the oracle."""
+    from musc_b200 import ops
+    n, p, c = 12, 49, 64
+    base = torch.randn(7, c, generator=torch.Generator().manual_seed(12))
+    z = base[torch.arange(n * p) % 7].reshape(n, p, c)
+    z = z + 1e-4 * torch.randn(n, p, c, generator=torch.Generator().manual_seed(13))
+    z = (z / z.norm(dim=-1, keepdim=True)).contiguous()
+    got = ops.msm(z.to(cuda_device), 0, n - 1).cpu().numpy()
+    want = omsm.msm(z.numpy(), 0, n - 1)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=2e-3)   # near-zero distances: see above
+    assert _lib_device_error_clear()
+
+
+def test_msm_screen_path_equals_exact_path_config2_bank(cuda_device, monkeypatch):
+    """One config-2 bank (N = 100, C = 1024, LNAMD r = 3): the default screen + refinement
+    and the 3-pass exact kernel give the same scores within fp32 rounding."""
+    from musc_b200 import ops
+    from musc_b200.synthetic import prototype_mixture_layer
+    tokens = prototype_mixture_layer(100, generator=torch.Generator().manual_seed(5))
+    z = ops.lnamd(tokens.to(cuda_device), (3,), l2_normalize=True)[0]
+    deferred = ops.msm(z)
+    monkeypatch.setenv('MUSC_B200_MSM_EXACT', '1')
+    exact = ops.msm(z)
+    torch.testing.assert_close(deferred, exact, rtol=2e-6, atol=0)
+    assert _lib_device_error_clear()
