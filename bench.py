@@ -65,6 +65,9 @@ def _args():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--collective-sms', type=int, default=0,
                     help='SMs left free for NCCL during each bank GEMM (multi-GPU; 0 = none)')
+    ap.add_argument('--exchange', default='copy', choices=['copy', 'nccl'],
+                    help='multi-GPU transport of banks and screen tables: peer copies on copy engines '
+                         '(default) or NCCL collectives')
     return ap.parse_args()
 
 
@@ -397,6 +400,11 @@ def run_b200(args):
                 layers[li].append(t)
         return [torch.cat(t) if t else torch.empty(0, 1 + P, C, device=dev) for t in layers]
 
+    exchange = None
+    if group is not None and args.exchange == 'copy':
+        from musc_b200.exchange import PeerExchange
+        exchange = PeerExchange(group, dev, pool, p_score, C)
+
     def step(inputs, ready=None):
         # NVTX range "pool_step": lets a profiler capture the launches of the pool steps only
         # (ncu --nvtx --nvtx-include "pool_step/"), not the synthetic-input generation
@@ -404,7 +412,7 @@ def run_b200(args):
         try:
             return pipeline.score_pool(tokens_of(inputs), n_images=pool, radii=radii, group=group, kernels=kern,
                                        super_fast_side=sf, ready=None if encoder is not None else ready,
-                                       collective_sms=args.collective_sms)
+                                       collective_sms=args.collective_sms, exchange=exchange)
         finally:
             torch.cuda.nvtx.range_pop()
 
@@ -516,7 +524,7 @@ def run_b200(args):
     parity = None
     if group is not None:
         res = pipeline.score_pool(tokens_of(resident), n_images=pool, radii=radii, group=group, kernels=ops,
-                                  super_fast_side=sf, verify=True)
+                                  super_fast_side=sf, verify=True, exchange=exchange)
         parity = res.verified
         torch.cuda.synchronize()
         ops.check_device_error(dev, 'bench parity')
@@ -550,7 +558,8 @@ def run_b200(args):
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
             'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-            'config': config_of(args, cfg, pool, world),
+            'config': dict(config_of(args, cfg, pool, world),
+                           **({'exchange': args.exchange} if world > 1 else {})),
             'e2e': {'value': pool / (e2e_ms / args.steps / 1e3), 'unit': UNIT,
                     'h2d_bytes_per_step': h2d * world, 'd2h_bytes_per_step': d2h},
             'roofline': {'kernel': ('nearest_kernel<symmetric>' if exact_path
@@ -591,6 +600,8 @@ def run_b200(args):
                                     'timed_s': round(m['wall_s'], 2)}
         print(json.dumps(line), flush=True)
     if group is not None:
+        if exchange is not None:
+            exchange.close()
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 

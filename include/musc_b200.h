@@ -326,6 +326,36 @@ int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* o
                             int batch, int tokens, int heads, int head_dim, long long qkv_row_stride,
                             long long out_row_stride, float scale, musc_b200_stream stream);
 
+/* ------------------------------------------------------------------------
+ * Copy-engine exchange between the GPUs of one node (multi-GPU pool scoring;
+ * no counterpart in the reference, which is single-device).
+ *
+ * musc_b200_ipc_get: the 64-byte CUDA IPC handle of the allocation holding
+ *     device pointer `ptr` and the offset of `ptr` inside it.
+ * musc_b200_ipc_open: maps a peer's handle into this process (peer access
+ *     enabled lazily); *base is what musc_b200_ipc_close takes, *ptr = *base +
+ *     offset.  A mapped pointer is only ever a cudaMemcpyAsync source or a
+ *     flag address here -- never a kernel or library operand.
+ * musc_b200_stream_signal: stream-ordered write of `value` to a 32-bit flag
+ *     (this device's or a peer's mapped memory); the stream's prior work is
+ *     made visible first.
+ * musc_b200_stream_wait: the stream waits until the flag (this device's
+ *     memory) is >= value (cyclic 32-bit comparison).  Counters only grow.
+ * musc_b200_copy_async: cudaMemcpyAsync of `bytes` between two device
+ *     pointers of the unified address space (peer copies run on copy engines).
+ * ---------------------------------------------------------------------- */
+int musc_b200_ipc_get(const void* ptr, void* handle, size_t* offset);
+
+int musc_b200_ipc_open(const void* handle, size_t offset, void** base, void** ptr);
+
+int musc_b200_ipc_close(void* base);
+
+int musc_b200_stream_signal(unsigned int* flag, unsigned int value, musc_b200_stream stream);
+
+int musc_b200_stream_wait(const unsigned int* flag, unsigned int value, musc_b200_stream stream);
+
+int musc_b200_copy_async(void* dst, const void* src, size_t bytes, musc_b200_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,12 @@ SIGNATURES = {
                                     ctypes.POINTER(_int), ctypes.c_double, ctypes.c_double, _int, _vp, _vp,
                                     _vp, _vp, _sz, _vp]),
     'musc_b200_score_maps': (_int, [_vp, _int, _int, _int, _int, _int, _vp, _vp, _vp, _vp]),
+    'musc_b200_ipc_get': (_int, [_vp, _vp, ctypes.POINTER(_sz)]),
+    'musc_b200_ipc_open': (_int, [_vp, _sz, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    'musc_b200_ipc_close': (_int, [_vp]),
+    'musc_b200_stream_signal': (_int, [_vp, ctypes.c_uint, _vp]),
+    'musc_b200_stream_wait': (_int, [_vp, ctypes.c_uint, _vp]),
+    'musc_b200_copy_async': (_int, [_vp, _vp, _sz, _vp]),
 }
 
 _lock = threading.Lock()

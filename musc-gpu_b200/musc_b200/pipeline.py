@@ -63,7 +63,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
                radii: Sequence[int] = (1, 3, 5), topmin_min: float = 0, topmin_max: float = 0.3,
                image_size: int = 518, super_fast_side: int | None = None,
                group=None, kernels=ops, ready: Sequence | None = None,
-               collective_sms: int = 0, verify: bool = False) -> PoolScores:
+               collective_sms: int = 0, verify: bool = False, exchange=None) -> PoolScores:
     """Score one pool from device-resident tokens.
 
     ``tokens``: per hooked layer, this rank's ``(n_local, 1+P, C)`` tokens
@@ -80,6 +80,9 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     GEMM so the neighbouring banks' gather and exchange run alongside it
     (0 = none, the default: the GEMM's dynamic tile scheduler already lets a
     collective that starts first keep its SMs).
+    ``exchange``: with a process group, a :class:`musc_b200.exchange.PeerExchange` of this
+    pool's shape: the banks and the screen tables then move between the GPUs by peer
+    copies on copy engines (no SMs, overlapping the GEMMs) instead of NCCL collectives.
     ``verify``: with a process group, re-score the last bank on every rank as one
     whole-pool part from the gathered bank and compare the rows each rank owns
     with the sharded result, bit for bit; the outcome (summed over ranks) is in
@@ -172,6 +175,11 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
                 kernels.screen_pool(bank, rows, c, p, 0, 1, rows, out=screen)
                 kernels.refine(bank, rows, c, p, 0, rows, b, screen[0], screen[1], out=table[0])
             select(table[0], li, ri)
+    elif exchange is not None and not exact_path:
+        if not exchange.matches(n_images, p, c, world):
+            raise ValueError('score_pool: the exchange was created for another pool shape')
+        verified = _score_with_exchange(kernels, exchange, banks, aggregate, local, select, rows, c, p, rank,
+                                        world, first, q_rows, a, b, scores, verify, group, n_images)
     else:
         local_rows, bank_rows = per * p, world * per * p
         sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
@@ -258,6 +266,55 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         maps = torch.empty(0, side, side, dtype=torch.float64, device=dev)
         image_max = torch.empty(0, dtype=torch.float64, device=dev)
     return PoolScores(scores, maps, image_max, first, n_images, verified)
+
+
+def _score_with_exchange(kernels, ex, banks, aggregate, local, select, rows, c, p, rank, world, first, q_rows,
+                         a, b, scores, verify, group, n_images):
+    """The multi-GPU bank loop over peer copies.  Compute-stream order per bank k:
+    prep k+1 (its copies then run under GEMM k), wait for bank k's copies, screen k, the
+    refinement of bank k-1 (its table copies ran under GEMM k), and so on."""
+    dev = scores.device
+    compute = torch.cuda.current_stream(dev)
+    exact_t = torch.empty(n_images, max(q_rows, 1), dtype=torch.float32, device=dev)
+
+    def start(k):
+        li, ri = banks[k]
+        aggregate(li)
+        v = ex.begin_bank()
+        lb = ex.local_bank_for(v, compute)
+        kernels.prep_bank(local[li, ri].reshape(ex.local_rows, c), out=lb)
+        full, events = ex.gather(v, compute)
+        return v, k, full, events
+
+    def finish(item):
+        v, k, full, k1, m2, events = item
+        for e in events:
+            compute.wait_event(e)
+        if q_rows:
+            kernels.refine(full, rows, c, p, first * p, q_rows, b, k1, m2, out=exact_t, bank_rows=ex.bank_rows)
+            select(exact_t, *banks[k])
+        ex.release(v, compute)
+
+    cur = start(0)
+    pending = None
+    for k in range(len(banks)):
+        nxt = start(k + 1) if k + 1 < len(banks) else None
+        v, _, full, events = cur
+        for e in events:
+            compute.wait_event(e)
+        scr = ex.screen_for(v, compute)
+        kernels.screen_pool(full, rows, c, p, rank, world, ex.rpb, out=scr, bank_rows=ex.bank_rows)
+        k1, m2, xevents = ex.exchange(v, compute)
+        if pending is not None:
+            finish(pending)
+        pending = (v, k, full, k1, m2, xevents)
+        cur = nxt
+    finish(pending)
+    if not verify:
+        return None
+    # the last bank's pool bank stays intact until the next call's third bank
+    return _verify_last_bank(kernels, ex.full_bank[pending[0] % 3], ex.bank_rows, rows, c, p, n_images, first,
+                             q_rows, a, b, scores[banks[-1][1], banks[-1][0]], banks[-1], group, False)
 
 
 def _verify_last_bank(kernels, bank, bank_rows, rows, c, p, n_images, first, q_rows, a, b, got, bank_id, group,

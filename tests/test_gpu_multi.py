@@ -1,9 +1,12 @@
-"""Multi-GPU parity: the sharded pipeline on 2 GPUs (NCCL) against the reference's golden pool.
+"""Multi-GPU parity: the sharded pipeline on 2 GPUs against the reference's golden pool.
 
-Each rank aggregates its query images, the banks are all-gathered, every rank evaluates
-its part of the symmetric tiles and a MIN reduce-scatter returns its rows' minima.  The
-gathered maps and image maxima must match the reference (config 1, N=16) within 2e-5
-relative, exactly like the single-GPU pipeline.  Skipped when fewer than 2 GPUs are visible.
+Each rank aggregates its query images, the banks are gathered, every rank screens its
+part of the symmetric tiles, the partial screen tables of each rank's rows are exchanged
+and refined.  Both transports are checked -- NCCL collectives, and peer copies on copy
+engines ordered by device-memory flags (``musc_b200.exchange``), over two pool steps so
+the flags' counters carry across calls.  The gathered maps and image maxima must match
+the reference (config 1, N=16) within 2e-5 relative, and the two transports must agree
+bit for bit.  Skipped when fewer than 2 GPUs are visible.
 """
 from __future__ import annotations
 
@@ -43,11 +46,20 @@ def _rank(rank, world, port, queue):
         g = golden('pool16')
         n = int(g['n'])
         tokens = prototype_mixture(n, n_layers=4, c=1024, side=37, seed=int(g['seed']))
+        from musc_b200.exchange import PeerExchange
         first, end, _ = shard_range(n, world, rank)
-        res = score_pool([t[first:end].to(dev) for t in tokens], n_images=n, group=dist.group.WORLD)
+        mine = [t[first:end].to(dev) for t in tokens]
+        res = score_pool(mine, n_images=n, group=dist.group.WORLD)
         maps, mx = gather_pool(res, dist.group.WORLD)
+        ex = PeerExchange(dist.group.WORLD, dev, n, 1369, 1024)
+        copies = []
+        for _ in range(2):                       # two steps: counters carry across calls
+            r2 = score_pool(mine, n_images=n, group=dist.group.WORLD, exchange=ex, verify=True)
+            m2, x2 = gather_pool(r2, dist.group.WORLD)
+            copies.append((m2.cpu().numpy(), x2.cpu().numpy(), r2.verified))
+        ex.close()
         if rank == 0:
-            queue.put((maps.cpu().numpy(), mx.cpu().numpy()))
+            queue.put((maps.cpu().numpy(), mx.cpu().numpy(), copies))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -66,9 +78,13 @@ def test_sharded_pool16_matches_reference(cuda_device, world):
     procs = [ctx.Process(target=_rank, args=(r, world, port, queue)) for r in range(world)]
     for p in procs:
         p.start()
-    maps, mx = queue.get(timeout=300)
+    maps, mx, copies = queue.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     np.testing.assert_allclose(maps, g['maps'], rtol=RTOL, atol=0)
     np.testing.assert_allclose(mx, g['image_max'], rtol=RTOL, atol=0)
+    for m2, x2, verified in copies:
+        np.testing.assert_array_equal(m2, maps)
+        np.testing.assert_array_equal(x2, mx)
+        assert verified['bit_exact']
