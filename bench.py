@@ -342,8 +342,8 @@ def run_b200(args):
     # ---- our kernels, instrumented: launch counts and the dominant kernel's event timing
     near_events, launches = [], [0]
     # our kernels per call: lnamd = statistics + stencil; nearest_pool = fill + GEMM; screen_pool = GEMM
-    # (its fills are memsets); refine = image bounds, refinement, fallback plan, gather, gathered GEMM,
-    # rescue
+    # (its fills are memsets); refine = image bounds + refinement + 3 per fallback round (plan, gather,
+    # gathered GEMM), counted by the library
     per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'prep_bank': 1, 'nearest_pool': 2, 'screen_pool': 1,
                 'refine': 6, 'trimmed_mean': 1, 'score_maps': 1}
     gemm_ops = ('nearest_pool', 'screen_pool')
@@ -362,7 +362,10 @@ def run_b200(args):
         fn = getattr(ops, name)
 
         def call(*a, **k):
-            launches[0] += per_call[name]
+            if name == 'refine':   # 2 kernels + 3 per fallback round (args: bank, rows, c, p, first, q_rows, ...)
+                launches[0] += ops.refine_launches(a[1] // a[3], a[5], a[2])
+            else:
+                launches[0] += per_call[name]
             st = torch.cuda.current_stream(dev)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)

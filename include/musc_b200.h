@@ -234,9 +234,19 @@ int musc_b200_screen_pool(const void* bank, long long bank_rows, long long rows,
  *     second-smallest screened value rules out every other patch, else the
  *     exact 3-pass minimum over the image's patches.
  * So musc_b200_trimmed_mean over exact_sq gives the reference's scores for any
- * rank_lo < rank_hi.  Scratch in `workspace` (musc_b200_refine_bytes, 1024-
- * byte aligned). */
+ * rank_lo < rank_hi.  Scratch in `workspace` (1024-byte aligned): its fixed
+ * part (the queue of uncertified pairs, n_images * query_rows ints) plus a
+ * staging bank for the exact fallback, which runs in rounds of as many rows as
+ * the staging bank holds.  musc_b200_refine_bytes is the default size (up to 2 M
+ * staged rows); any size >= musc_b200_refine_min_bytes (128 staged rows) gives
+ * the same results in more rounds. */
 size_t musc_b200_refine_bytes(int n_images, long long query_rows, int channels);
+
+size_t musc_b200_refine_min_bytes(int n_images, long long query_rows, int channels);
+
+/* Kernels one musc_b200_refine call with this workspace size enqueues (2 plus 3 per
+ * fallback round; rounds past the end of the queue return at once). */
+int musc_b200_refine_launches(int n_images, long long query_rows, int channels, size_t workspace_bytes);
 
 int musc_b200_refine(const void* bank, long long bank_rows, long long rows, int channels,
                      int patches_per_image, long long first_row, long long query_rows, int rank_hi,

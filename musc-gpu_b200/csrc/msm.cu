@@ -38,10 +38,12 @@ namespace musc {
 
 // Implemented in refine.cu.
 size_t refine_workspace_bytes(int n_images, long long q_rows, int channels);
+size_t refine_min_workspace_bytes(int n_images, long long q_rows, int channels);
+long long refine_rounds(int n_images, long long q_rows, int channels, size_t bytes);
 int refine_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
                   long long first_row, long long q_rows, int rank_hi, const unsigned long long* k1,
                   const unsigned int* m2, int n_parts, long long part_stride, long long table_rows,
-                  float* exact, void* workspace, cudaStream_t s);
+                  float* exact, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -655,6 +657,17 @@ extern "C" size_t musc_b200_refine_bytes(int n_images, long long query_rows, int
   return refine_workspace_bytes(n_images, query_rows, channels);
 }
 
+extern "C" int musc_b200_refine_launches(int n_images, long long query_rows, int channels,
+                                         size_t workspace_bytes) {
+  if (n_images <= 0 || query_rows <= 0 || channels <= 0) return 0;
+  return (int)(2 + 3 * refine_rounds(n_images, query_rows, channels, workspace_bytes));
+}
+
+extern "C" size_t musc_b200_refine_min_bytes(int n_images, long long query_rows, int channels) {
+  if (n_images <= 0 || query_rows <= 0 || channels <= 0) return 0;
+  return refine_min_workspace_bytes(n_images, query_rows, channels);
+}
+
 extern "C" int musc_b200_refine(const void* bank, long long bank_rows, long long rows, int channels,
                                 int patches_per_image, long long first_row, long long query_rows, int rank_hi,
                                 const void* k1, const void* m2, int n_partials, long long partial_stride,
@@ -677,12 +690,13 @@ extern "C" int musc_b200_refine(const void* bank, long long bank_rows, long long
     return fail(MUSC_B200_ERR_INVALID, "refine: query rows must lie in the pool and in the tables");
   if (n_partials <= 0 || (n_partials > 1 && partial_stride < (long long)n_images * table_rows))
     return fail(MUSC_B200_ERR_INVALID, "refine: partial tables overlap");
-  if (workspace_bytes < refine_workspace_bytes(n_images, query_rows, channels))
-    return fail(MUSC_B200_ERR_WORKSPACE, "refine: workspace smaller than musc_b200_refine_bytes");
+  if (workspace_bytes < refine_min_workspace_bytes(n_images, query_rows, channels))
+    return fail(MUSC_B200_ERR_WORKSPACE, "refine: workspace smaller than musc_b200_refine_min_bytes");
   MUSC_TRY(require_sm100());
   return refine_launch(bank, bank_rows, rows, channels, patches_per_image, first_row, query_rows, rank_hi,
                        static_cast<const unsigned long long*>(k1), static_cast<const unsigned int*>(m2), n_partials,
-                       partial_stride, table_rows, exact_sq, workspace, reinterpret_cast<cudaStream_t>(stream));
+                       partial_stride, table_rows, exact_sq, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 // MUSC_B200_MSM_EXACT=1 in the environment selects the 3-pass symmetric kernel for every

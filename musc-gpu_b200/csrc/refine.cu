@@ -23,9 +23,8 @@
 //   3. fallback_plan_kernel / fallback_gather_kernel: the queued rows are
 //      copied, image by image, into a staging bank (128-row tiles), and
 //      nearest_kernel<GATHER> evaluates each tile exactly (3-pass split fp16)
-//      against its image, lowering the table entries with atomic minima.
-//   4. rescue_kernel: rows of images that did not fit the staging bank (only
-//      in pathological pools) are evaluated exactly in fp32, patch by patch.
+//      against its image, lowering the table entries with atomic minima -- in
+//      rounds of at most the staging bank's capacity, until the queue is drained.
 // The interval average then runs on the exact table as before.
 //
 // Error bound of a screened distance (original units, a = query, b = reference,
@@ -56,7 +55,6 @@ namespace {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 constexpr int kRefineThreads = 256;  // 8 warps
-constexpr int kPlanThreads = 1024;
 
 struct BankPlanes {
   const __half* hi;
@@ -77,37 +75,56 @@ BankPlanes bank_planes(const void* bank, long long bank_rows, int channels) {
 }
 
 // Workspace of one refinement (rank-local rows): the queue, the staging bank and the
-// small planning arrays.  Offsets in bytes, each 1024-aligned.
+// small planning arrays.  Offsets in bytes, each 1024-aligned.  The staging bank holds
+// `cap` rows; the fallback stages the queue in rounds of at most `cap` rows, so any
+// capacity >= 128 rows works (a smaller workspace means more rounds).
 struct RefineLayout {
-  size_t bounds, counts, seg_start, lists, tile_img, row_map, s_norm, s_inv, s_hi, s_lo, words, total;
+  size_t bounds, counts, lists, words, tile_img, tile_off, row_map, s_norm, s_inv, s_hi, s_lo, total;
   long long cap;  // staging rows (multiple of 128)
 };
 
-long long staging_rows(int n_images, long long q_rows) {
-  const long long full = (long long)n_images * q_rows;              // every pair queued
-  long long cap = 4 * q_rows + 128LL * n_images;                     // 4 queued images per row on average
-  cap = std::min(cap, full + 128LL * n_images);
-  return (cap + 127) / 128 * 128;
+constexpr long long kMaxStagingRows = 1LL << 21;  // 2 M rows: 8 GB of hi + lo at C = 1024
+
+// Default staging capacity: 4 queued images per row on average (far above the typical
+// certified fraction), at most every pair plus padding, at most kMaxStagingRows.
+long long default_staging_rows(int n_images, long long q_rows) {
+  const long long full = (long long)n_images * q_rows + 128LL * n_images;
+  long long cap = std::min(4 * q_rows + 128LL * n_images, full);
+  cap = std::min(cap, kMaxStagingRows);
+  return std::max(128LL, (cap + 127) / 128 * 128);
 }
 
-RefineLayout refine_layout(int n_images, long long q_rows, int channels) {
+RefineLayout refine_layout(int n_images, long long q_rows, int channels, long long cap) {
   RefineLayout l;
-  l.cap = staging_rows(n_images, q_rows);
+  l.cap = cap;
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes, 1024); return at; };
   l.bounds = take((size_t)n_images * 4 * sizeof(float));
   l.counts = take((size_t)n_images * sizeof(int));
-  l.seg_start = take((size_t)n_images * sizeof(long long));
   l.lists = take((size_t)n_images * q_rows * sizeof(int));
-  l.tile_img = take((size_t)(l.cap / nearest::CTA_M) * sizeof(int));
-  l.row_map = take((size_t)l.cap * sizeof(int));
-  l.s_norm = take((size_t)l.cap * sizeof(float));
-  l.s_inv = take((size_t)l.cap * sizeof(float));
-  l.s_hi = take((size_t)l.cap * channels * 2);
-  l.s_lo = take((size_t)l.cap * channels * 2);
-  l.words = take(4 * sizeof(long long));  // tile_total, staged_rows, scheduler, spare
+  l.words = take(8 * sizeof(long long));  // tiles, staged rows, scheduler, cursor image, cursor offset
+  l.tile_img = take((size_t)(cap / nearest::CTA_M) * sizeof(int));
+  l.tile_off = take((size_t)(cap / nearest::CTA_M) * sizeof(int));
+  l.row_map = take((size_t)cap * sizeof(int));
+  l.s_norm = take((size_t)cap * sizeof(float));
+  l.s_inv = take((size_t)cap * sizeof(float));
+  l.s_hi = take((size_t)cap * channels * 2);
+  l.s_lo = take((size_t)cap * channels * 2);
   l.total = o;
   return l;
+}
+
+// The largest staging capacity (multiple of 128, at most the default) whose layout fits
+// `bytes`; 0 when even 128 rows do not fit.
+long long staging_rows_for(int n_images, long long q_rows, int channels, size_t bytes) {
+  long long hi = default_staging_rows(n_images, q_rows) / 128, lo = 0;
+  if (refine_layout(n_images, q_rows, channels, hi * 128).total <= bytes) return hi * 128;
+  while (hi - lo > 1) {
+    const long long mid = (lo + hi) / 2;
+    if (refine_layout(n_images, q_rows, channels, mid * 128).total <= bytes) lo = mid;
+    else hi = mid;
+  }
+  return lo * 128;
 }
 
 // ------------------------------------------------------------------ image bounds
@@ -172,6 +189,7 @@ __device__ float exact_d2(const BankPlanes& b, long long qa, long long pb, int c
   const __half* hb = b.hi + pb * channels;
   const __half* lb = b.lo + pb * channels;
   float acc = 0.f;
+#pragma unroll 4
   for (int c = lane * 8; c < channels; c += 256) {
     const uint4 vha = __ldg(reinterpret_cast<const uint4*>(ha + c));
     const uint4 vla = __ldg(reinterpret_cast<const uint4*>(la + c));
@@ -190,6 +208,46 @@ __device__ float exact_d2(const BankPlanes& b, long long qa, long long pb, int c
     }
   }
   return warp_sum(acc);
+}
+
+// The same for two reference rows at once (the query row's loads shared): twice the
+// loads in flight per warp, for the latency-bound gathers of the refinement.
+__device__ void exact_d2_pair(const BankPlanes& b, long long qa, long long p0, long long p1, int channels, int lane,
+                              float* d0, float* d1) {
+  const float ia = __ldg(b.inv + qa), i0 = __ldg(b.inv + p0), i1 = __ldg(b.inv + p1);
+  const __half* ha = b.hi + qa * channels;
+  const __half* la = b.lo + qa * channels;
+  const __half* h0 = b.hi + p0 * channels;
+  const __half* l0 = b.lo + p0 * channels;
+  const __half* h1 = b.hi + p1 * channels;
+  const __half* l1 = b.lo + p1 * channels;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+  for (int c = lane * 8; c < channels; c += 256) {
+    const uint4 vha = __ldg(reinterpret_cast<const uint4*>(ha + c));
+    const uint4 vla = __ldg(reinterpret_cast<const uint4*>(la + c));
+    const uint4 vh0 = __ldg(reinterpret_cast<const uint4*>(h0 + c));
+    const uint4 vl0 = __ldg(reinterpret_cast<const uint4*>(l0 + c));
+    const uint4 vh1 = __ldg(reinterpret_cast<const uint4*>(h1 + c));
+    const uint4 vl1 = __ldg(reinterpret_cast<const uint4*>(l1 + c));
+    const __half* pha = reinterpret_cast<const __half*>(&vha);
+    const __half* pla = reinterpret_cast<const __half*>(&vla);
+    const __half* ph0 = reinterpret_cast<const __half*>(&vh0);
+    const __half* pl0 = reinterpret_cast<const __half*>(&vl0);
+    const __half* ph1 = reinterpret_cast<const __half*>(&vh1);
+    const __half* pl1 = reinterpret_cast<const __half*>(&vl1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float xa = (__half2float(pha[e]) + __half2float(pla[e])) * ia;
+      const float x0 = (__half2float(ph0[e]) + __half2float(pl0[e])) * i0;
+      const float x1 = (__half2float(ph1[e]) + __half2float(pl1[e])) * i1;
+      const float e0 = xa - x0, e1 = xa - x1;
+      a0 = fmaf(e0, e0, a0);
+      a1 = fmaf(e1, e1, a1);
+    }
+  }
+  *d0 = warp_sum(a0);
+  *d1 = warp_sum(a1);
 }
 
 __global__ void __launch_bounds__(kRefineThreads)
@@ -291,14 +349,11 @@ refine_kernel(const RefineParams rp) {
         }
       }
       uint32_t mask = __ballot_sync(0xffffffffu, need);
-      while (mask) {
-        const int src = __ffs(mask) - 1;
-        mask &= mask - 1;
-        const int jj = jb + src;
-        const unsigned long long k = kr[jj];
-        const long long prow = (long long)jj * rp.patches + (long long)(uint32_t)k;
-        const float d = fmaxf(exact_d2(rp.bank, grow, prow, rp.channels, lane), 0.f);
+      // The exact distance to each needed image's screened argmin, two images at a time;
+      // the lane that owns the image stores it and decides its certification.
+      auto settle = [&](int src, float d) {
         if (lane == src) {
+          const int jj = jb + src;
           xr[jj] = d;
           const float m2v = __uint_as_float(mr[jj]);
           const bool certified = mr[jj] == (nearest::UMAX & ~0xFFu) || m2v * lo_scale - e >= d;
@@ -306,6 +361,22 @@ refine_kernel(const RefineParams rp) {
             const int slot = atomicAdd(rp.counts + jj, 1);
             rp.lists[(long long)jj * rp.q_rows + slot] = (int)q;
           }
+        }
+      };
+      while (mask) {
+        const int s0 = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const long long p0 = (long long)(jb + s0) * rp.patches + (long long)(uint32_t)kr[jb + s0];
+        if (mask) {
+          const int s1 = __ffs(mask) - 1;
+          mask &= mask - 1;
+          const long long p1 = (long long)(jb + s1) * rp.patches + (long long)(uint32_t)kr[jb + s1];
+          float d0, d1;
+          exact_d2_pair(rp.bank, grow, p0, p1, rp.channels, lane, &d0, &d1);
+          settle(s0, fmaxf(d0, 0.f));
+          settle(s1, fmaxf(d1, 0.f));
+        } else {
+          settle(s0, fmaxf(exact_d2(rp.bank, grow, p0, rp.channels, lane), 0.f));
         }
       }
     }
@@ -320,68 +391,40 @@ refine_kernel(const RefineParams rp) {
   }
 }
 
-// ------------------------------------------------------------------ fallback planning
-// One CTA: 128-row tiles per queued image, laid out image after image in the staging
-// bank while they fit; images that do not fit keep seg_start = -1 (rescue kernel).
-// words[0] = tiles for the GATHER kernel (m-tiles x nsub), words[1] = staged rows.
-__global__ void __launch_bounds__(kPlanThreads)
-fallback_plan_kernel(const int* __restrict__ counts, int n_images, long long cap_tiles, int nsub,
-                     long long* __restrict__ seg_start, int* __restrict__ tile_img, long long* __restrict__ words) {
-  __shared__ long long scan[kPlanThreads];
-  __shared__ long long carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  for (int base = 0; base < n_images; base += kPlanThreads) {
-    const int j = base + threadIdx.x;
-    const long long t = j < n_images ? (counts[j] + nearest::CTA_M - 1) / nearest::CTA_M : 0;
-    scan[threadIdx.x] = t;
-    __syncthreads();
-    for (int off = 1; off < kPlanThreads; off <<= 1) {  // inclusive scan
-      const long long v = threadIdx.x >= off ? scan[threadIdx.x - off] : 0;
-      __syncthreads();
-      scan[threadIdx.x] += v;
-      __syncthreads();
+// ------------------------------------------------------------------ fallback rounds
+// One thread: the next round's 128-row tiles, image after image from the cursor
+// (words[3] = image, words[4] = offset in its queue) until the staging bank is full.
+// tile_img / tile_off: each tile's image and the queue offset of its first row;
+// words[0] = tiles x nsub for the GATHER kernel, words[1] = staged rows, words[2] = the
+// GATHER kernel's scheduler (zeroed).  A round after the last does nothing.
+__global__ void fallback_plan_kernel(const int* __restrict__ counts, int n_images, long long cap_tiles, int nsub,
+                                     int* __restrict__ tile_img, int* __restrict__ tile_off,
+                                     long long* __restrict__ words) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  long long j = words[3], off = words[4], tiles = 0;
+  while (j < n_images && tiles < cap_tiles) {
+    if (off >= counts[j]) {
+      ++j;
+      off = 0;
+      continue;
     }
-    const long long end = carry + scan[threadIdx.x];
-    const long long start = end - t;
-    if (j < n_images) {
-      if (t > 0 && end <= cap_tiles) {
-        seg_start[j] = start * nearest::CTA_M;
-        for (long long m = start; m < end; ++m) tile_img[m] = j;
-      } else {
-        seg_start[j] = t > 0 ? -1 : 0;
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == kPlanThreads - 1) carry = end;
-    __syncthreads();
+    tile_img[tiles] = (int)j;
+    tile_off[tiles] = (int)off;
+    ++tiles;
+    off += nearest::CTA_M;
   }
-  if (threadIdx.x == 0) {
-    // The staged prefix: every image whose tiles end within the capacity.  Images
-    // after the first one that does not fit are rescued too, so the staged tiles
-    // stay one contiguous prefix.
-    long long staged_tiles = 0;
-    bool cut = false;
-    for (int j = 0; j < n_images; ++j) {
-      const long long t = (counts[j] + nearest::CTA_M - 1) / nearest::CTA_M;
-      if (t == 0) continue;
-      if (cut || staged_tiles + t > cap_tiles) {
-        cut = true;
-        seg_start[j] = -1;
-        continue;
-      }
-      staged_tiles += t;
-    }
-    words[0] = staged_tiles * nsub;
-    words[1] = staged_tiles * nearest::CTA_M;
-  }
+  words[0] = tiles * nsub;
+  words[1] = tiles * nearest::CTA_M;
+  words[2] = 0;
+  words[3] = j;
+  words[4] = off;
 }
 
-// One warp per staged row: copy the queued row's hi and lo planes, |z|^2 and 2^-k from
-// the pool bank into the staging bank; padding rows get row_map = -1.
+// One warp per staged row of the round: copy the queued row's hi and lo planes, |z|^2
+// and 2^-k from the pool bank into the staging bank; padding rows get row_map = -1.
 __global__ void __launch_bounds__(256)
 fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const int* __restrict__ counts,
-                       const long long* __restrict__ seg_start, const int* __restrict__ tile_img,
+                       const int* __restrict__ tile_img, const int* __restrict__ tile_off,
                        const int* __restrict__ lists, long long q_rows, const long long* __restrict__ words,
                        __half* __restrict__ s_hi, __half* __restrict__ s_lo, float* __restrict__ s_norm,
                        float* __restrict__ s_inv, int* __restrict__ row_map) {
@@ -389,8 +432,9 @@ fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long s = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < staged; s += warps) {
-    const int j = tile_img[s / nearest::CTA_M];
-    const long long k = s - seg_start[j];
+    const long long mt = s / nearest::CTA_M;
+    const int j = tile_img[mt];
+    const long long k = tile_off[mt] + (s - mt * nearest::CTA_M);
     if (k >= counts[j]) {
       if (lane == 0) row_map[s] = -1;
       continue;
@@ -406,24 +450,6 @@ fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const
       s_inv[s] = __ldg(bank.inv + g);
       row_map[s] = q;
     }
-  }
-}
-
-// Queued rows of images that did not fit the staging bank: exact fp32 minimum over
-// every patch of the image, one warp per (image, row).  Idle unless the queue overflowed.
-__global__ void __launch_bounds__(256)
-rescue_kernel(BankPlanes bank, long long first_row, int channels, int patches, const int* __restrict__ counts,
-              const long long* __restrict__ seg_start, const int* __restrict__ lists, long long q_rows,
-              unsigned int* __restrict__ exact) {
-  const int j = blockIdx.x;
-  if (seg_start[j] >= 0) return;
-  const int lane = threadIdx.x & 31;
-  for (int k = threadIdx.x >> 5; k < counts[j]; k += blockDim.x >> 5) {
-    const int q = lists[(long long)j * q_rows + k];
-    float best = FLT_MAX;
-    for (int pt = 0; pt < patches; ++pt)
-      best = fminf(best, exact_d2(bank, first_row + q, (long long)j * patches + pt, channels, lane));
-    if (lane == 0) atomicMin(exact + (long long)j * q_rows + q, __float_as_uint(fmaxf(best, 0.f)));
   }
 }
 
@@ -443,23 +469,38 @@ int refine_rows_per_cta(int n_images, int* pitch, size_t* smem) {
 }  // namespace
 
 size_t refine_workspace_bytes(int n_images, long long q_rows, int channels) {
-  return refine_layout(n_images, q_rows, channels).total;
+  return refine_layout(n_images, q_rows, channels, default_staging_rows(n_images, q_rows)).total;
+}
+
+size_t refine_min_workspace_bytes(int n_images, long long q_rows, int channels) {
+  return refine_layout(n_images, q_rows, channels, 128).total;
+}
+
+// Fallback rounds enqueued for a workspace of `bytes`: enough for every (row, image) pair.
+long long refine_rounds(int n_images, long long q_rows, int channels, size_t bytes) {
+  const long long cap = staging_rows_for(n_images, q_rows, channels, bytes);
+  if (cap < 128) return 0;
+  const long long worst_tiles = ((long long)n_images * q_rows) / nearest::CTA_M + n_images;
+  const long long cap_tiles = cap / nearest::CTA_M;
+  return (worst_tiles + cap_tiles - 1) / cap_tiles;
 }
 
 // The whole refinement of one bank for rows [first_row, first_row + q_rows) of the pool.
 int refine_launch(const void* bank, long long bank_rows, long long rows, int channels, int patches,
                   long long first_row, long long q_rows, int rank_hi, const unsigned long long* k1,
                   const unsigned int* m2, int n_parts, long long part_stride, long long table_rows,
-                  float* exact, void* workspace, cudaStream_t s) {
+                  float* exact, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   const int n_images = (int)(rows / patches);
-  const RefineLayout l = refine_layout(n_images, q_rows, channels);
+  const long long cap = staging_rows_for(n_images, q_rows, channels, workspace_bytes);
+  if (cap < 128) return fail(MUSC_B200_ERR_WORKSPACE, "refine: workspace below musc_b200_refine_min_bytes");
+  const RefineLayout l = refine_layout(n_images, q_rows, channels, cap);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const BankPlanes bp = bank_planes(bank, bank_rows, channels);
   float* bounds = reinterpret_cast<float*>(ws + l.bounds);
   int* counts = reinterpret_cast<int*>(ws + l.counts);
-  long long* seg_start = reinterpret_cast<long long*>(ws + l.seg_start);
   int* lists = reinterpret_cast<int*>(ws + l.lists);
   int* tile_img = reinterpret_cast<int*>(ws + l.tile_img);
+  int* tile_off = reinterpret_cast<int*>(ws + l.tile_off);
   int* row_map = reinterpret_cast<int*>(ws + l.row_map);
   float* s_norm = reinterpret_cast<float*>(ws + l.s_norm);
   float* s_inv = reinterpret_cast<float*>(ws + l.s_inv);
@@ -468,7 +509,7 @@ int refine_launch(const void* bank, long long bank_rows, long long rows, int cha
   long long* words = reinterpret_cast<long long*>(ws + l.words);
 
   MUSC_CUDA(cudaMemsetAsync(counts, 0, (size_t)n_images * sizeof(int), s));
-  MUSC_CUDA(cudaMemsetAsync(words, 0, 4 * sizeof(long long), s));
+  MUSC_CUDA(cudaMemsetAsync(words, 0, 8 * sizeof(long long), s));
   image_bounds_kernel<<<n_images, 256, 0, s>>>(bp.norm, bp.lnorm, patches, bounds);
   MUSC_TRY(check_launch("image_bounds_kernel"));
 
@@ -501,16 +542,12 @@ int refine_launch(const void* bank, long long bank_rows, long long rows, int cha
   refine_kernel<<<(unsigned)blocks, kRefineThreads, smem, s>>>(rp);
   MUSC_TRY(check_launch("refine_kernel"));
 
+  // Exact 3-pass evaluation of the queued rows against their images, in rounds of at
+  // most `cap` staged rows.  The host cannot see the queue's length without a
+  // synchronisation, so it enqueues the worst-case number of rounds; rounds after the
+  // queue is drained find nothing to plan and their kernels return at once.
   const int nsub = (patches + nearest::BN - 1) / nearest::BN;
-  fallback_plan_kernel<<<1, kPlanThreads, 0, s>>>(counts, n_images, l.cap / nearest::CTA_M, nsub, seg_start,
-                                                   tile_img, words);
-  MUSC_TRY(check_launch("fallback_plan_kernel"));
   const int sms = sm_count();
-  fallback_gather_kernel<<<sms * 4, 256, 0, s>>>(bp, first_row, channels, counts, seg_start, tile_img, lists,
-                                                  q_rows, words, s_hi, s_lo, s_norm, s_inv, row_map);
-  MUSC_TRY(check_launch("fallback_gather_kernel"));
-
-  // Exact 3-pass evaluation of the staged rows against their images.
   CUtensorMap mqh, mql, mrh, mrl;
   MUSC_TRY(make_plane_map(&mqh, s_hi, l.cap, channels, nearest::CTA_M, nearest::BK));
   MUSC_TRY(make_plane_map(&mql, s_lo, l.cap, channels, nearest::CTA_M, nearest::BK));
@@ -540,13 +577,21 @@ int refine_launch(const void* bank, long long bank_rows, long long rows, int cha
   p.num_kb = (channels + nearest::BK - 1) / nearest::BK;
   p.nsub = nsub;
   MUSC_TRY(set_nearest_smem_attrs());
-  nearest::nearest_kernel<nearest::GATHER, false>
-      <<<sms, nearest::Cfg<nearest::GATHER, false>::THREADS, nearest::smem_bytes<nearest::GATHER, false>(), s>>>(
-          mqh, mql, mrh, mrl, p);
-  MUSC_TRY(check_launch("nearest_kernel<gather>"));
-  rescue_kernel<<<n_images, 256, 0, s>>>(bp, first_row, channels, patches, counts, seg_start, lists, q_rows,
-                                         reinterpret_cast<unsigned int*>(exact));
-  return check_launch("rescue_kernel");
+  // worst case: every (row, image) pair queued, each image's queue padded to whole tiles
+  const long long cap_tiles = l.cap / nearest::CTA_M;
+  const long long rounds = refine_rounds(n_images, q_rows, channels, workspace_bytes);
+  for (long long r = 0; r < rounds; ++r) {
+    fallback_plan_kernel<<<1, 32, 0, s>>>(counts, n_images, cap_tiles, nsub, tile_img, tile_off, words);
+    MUSC_TRY(check_launch("fallback_plan_kernel"));
+    fallback_gather_kernel<<<sms * 4, 256, 0, s>>>(bp, first_row, channels, counts, tile_img, tile_off, lists,
+                                                    q_rows, words, s_hi, s_lo, s_norm, s_inv, row_map);
+    MUSC_TRY(check_launch("fallback_gather_kernel"));
+    nearest::nearest_kernel<nearest::GATHER, false>
+        <<<sms, nearest::Cfg<nearest::GATHER, false>::THREADS, nearest::smem_bytes<nearest::GATHER, false>(), s>>>(
+            mqh, mql, mrh, mrl, p);
+    MUSC_TRY(check_launch("nearest_kernel<gather>"));
+  }
+  return MUSC_B200_OK;
 }
 
 }  // namespace musc

@@ -41,6 +41,8 @@ SIGNATURES = {
     'musc_b200_bank_layout': (_int, [_ll, _int, ctypes.POINTER(_sz)]),
     'musc_b200_screen_pool': (_int, [_vp, _ll, _ll, _int, _int, _int, _int, _ll, _int, _vp, _vp, _vp, _vp]),
     'musc_b200_refine_bytes': (_sz, [_int, _ll, _int]),
+    'musc_b200_refine_min_bytes': (_sz, [_int, _ll, _int]),
+    'musc_b200_refine_launches': (_int, [_int, _ll, _int, _sz]),
     'musc_b200_refine': (_int, [_vp, _ll, _ll, _int, _int, _ll, _ll, _int, _vp, _vp, _int, _ll, _ll, _vp, _vp,
                                 _sz, _vp]),
     'musc_b200_trimmed_mean': (_int, [_vp, _ll, _int, _int, _int, _vp, _vp]),

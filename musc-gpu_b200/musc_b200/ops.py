@@ -250,14 +250,23 @@ def screen_pool(bank: torch.Tensor, rows: int, channels: int, patches: int, part
     return out
 
 
+def refine_launches(n_images: int, query_rows: int, channels: int, workspace_bytes: int | None = None) -> int:
+    """Kernels one :func:`refine` call enqueues (with the default workspace)."""
+    lib = _lib.lib()
+    ws = lib.musc_b200_refine_bytes(n_images, query_rows, channels) if workspace_bytes is None else workspace_bytes
+    return lib.musc_b200_refine_launches(n_images, query_rows, channels, ws)
+
+
 def refine(bank: torch.Tensor, rows: int, channels: int, patches: int, first_row: int, query_rows: int,
            rank_hi: int, k1: torch.Tensor, m2: torch.Tensor, out: torch.Tensor | None = None,
-           bank_rows: int | None = None) -> torch.Tensor:
+           bank_rows: int | None = None, workspace_bytes: int | None = None) -> torch.Tensor:
     """Exact squared minima ``(n_images, query_rows)`` float32 from screen tables.
 
     ``k1`` / ``m2``: ``(parts, n_images, table_rows)`` partial screen tables covering the
     query rows (local row = row - first_row), one per part of the pool's tile list.
     Images that cannot reach the trimmed ranks ``[.., rank_hi)`` hold FLT_MAX.
+    ``workspace_bytes``: the refinement's scratch (default ``musc_b200_refine_bytes``); any
+    size from ``musc_b200_refine_min_bytes`` up gives the same table in more fallback rounds.
     """
     dev = bank.device
     n_images = rows // patches
@@ -270,7 +279,8 @@ def refine(bank: torch.Tensor, rows: int, channels: int, patches: int, first_row
         out = torch.empty(n_images, query_rows, dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
         lib = _lib.lib()
-        ws_bytes = lib.musc_b200_refine_bytes(n_images, query_rows, channels)
+        ws_bytes = (lib.musc_b200_refine_bytes(n_images, query_rows, channels) if workspace_bytes is None
+                    else int(workspace_bytes))
         ws = _aligned_empty(ws_bytes, dev)
         st = lib.musc_b200_refine(_ptr(bank), rows if bank_rows is None else bank_rows, rows, channels, patches,
                                   first_row, query_rows, rank_hi, _ptr(k1), _ptr(m2), parts, n_images * table_rows,

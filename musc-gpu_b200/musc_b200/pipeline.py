@@ -111,11 +111,12 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     side = math.isqrt(p)
     n_r, n_l = len(radii), len(tokens)
 
-    # 1. LNAMD of the local images into (R*L) local banks, padded to `per` images
-    #    (only the padding is zeroed: it is gathered but never scored).
-    local = torch.empty(n_l, n_r, per, p, c, dtype=torch.float32, device=dev)
+    # 1. LNAMD of the local images into the R radii banks of one layer, padded to `per`
+    #    images (only the padding is zeroed: it is gathered but never scored).  Layer l+1's
+    #    LNAMD overwrites them; every bank of layer l is prepared (stream-ordered) before it.
+    local = torch.empty(n_r, per, p, c, dtype=torch.float32, device=dev)   # one layer's radii at a time
     if per > n_local:
-        local[:, :, n_local:].zero_()
+        local[:, n_local:].zero_()
     done = [False] * n_l
 
     def aggregate(li: int) -> None:
@@ -128,10 +129,10 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
             return
         t = tokens[li]
         if super_fast_side is not None:
-            kernels.lnamd_super_fast(t, super_fast_side, True, out=local[li, 0, :n_local],
+            kernels.lnamd_super_fast(t, super_fast_side, True, out=local[0, :n_local],
                                      image_stride=p * c, patch_stride=c)
         else:
-            kernels.lnamd(t, radii, True, out=[local[li, ri, :n_local] for ri in range(n_r)])
+            kernels.lnamd(t, radii, True, out=[local[ri, :n_local] for ri in range(n_r)])
 
     # 2. Per bank: prep, (gather), symmetric nearest minima, interval average.
     #    One GPU: prep the whole bank, one symmetric launch, select.
@@ -168,7 +169,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
             table = torch.empty(1, n_images, rows, dtype=torch.float32, device=dev)
         for li, ri in banks:
             aggregate(li)
-            kernels.prep_bank(local[li, ri, :n_images].reshape(rows, c), out=bank)
+            kernels.prep_bank(local[ri, :n_images].reshape(rows, c), out=bank)
             if exact_path:
                 kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, out=table)
             else:
@@ -193,7 +194,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         def start_gather(k):
             li, ri = banks[k]
             aggregate(li)
-            kernels.prep_bank(local[li, ri].reshape(local_rows, c), out=local_bank[k % 2])
+            kernels.prep_bank(local[ri].reshape(local_rows, c), out=local_bank[k % 2])
             pieces = zip(kernels.bank_planes(full_bank[k % 3], bank_rows, c),
                          kernels.bank_planes(local_bank[k % 2], local_rows, c))
             return [dist.all_gather_into_tensor(f, l, group=gather_group, async_op=True) for f, l in pieces]
@@ -282,7 +283,7 @@ def _score_with_exchange(kernels, ex, banks, aggregate, local, select, rows, c, 
         aggregate(li)
         v = ex.begin_bank()
         lb = ex.local_bank_for(v, compute)
-        kernels.prep_bank(local[li, ri].reshape(ex.local_rows, c), out=lb)
+        kernels.prep_bank(local[ri].reshape(ex.local_rows, c), out=lb)
         full, events = ex.gather(v, compute)
         return v, k, full, events
 

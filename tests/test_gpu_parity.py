@@ -491,19 +491,32 @@ def test_refine_combines_partial_screens_exactly(cuda_device, parts):
         assert torch.equal(got, whole[:, first * p:first * p + q_rows])
 
 
-def test_refine_rescue_when_the_staging_bank_overflows(cuda_device):
-    """A pool of repeated patches (every pair a tie, nothing certifiable) with the interval
-    reaching every image queues more rows than the staging bank holds; the overflow goes
-    through the exact fp32 rescue and the scores still match the oracle."""
-    from musc_b200 import ops
+def test_refine_fallback_rounds_with_a_small_workspace(cuda_device):
+    """A pool of repeated patches (every pair a near tie, nothing certifiable) with the
+    interval reaching every image queues every pair for the exact fallback.  With the
+    smallest workspace (a 128-row staging bank) the fallback runs in many rounds and must
+    give the default workspace's table bit for bit; the scores match the oracle."""
+    from musc_b200 import _lib, ops
     n, p, c = 12, 49, 64
     base = torch.randn(7, c, generator=torch.Generator().manual_seed(12))
     z = base[torch.arange(n * p) % 7].reshape(n, p, c)
     z = z + 1e-4 * torch.randn(n, p, c, generator=torch.Generator().manual_seed(13))
     z = (z / z.norm(dim=-1, keepdim=True)).contiguous()
-    got = ops.msm(z.to(cuda_device), 0, n - 1).cpu().numpy()
+    rows = n * p
+    bank = ops.prep_bank(z.reshape(rows, c).to(cuda_device))
+    k1, m2, _ = ops.screen_pool(bank, rows, c, p)
+    lib = _lib.lib()
+    small = lib.musc_b200_refine_min_bytes(n, rows, c)
+    assert small < lib.musc_b200_refine_bytes(n, rows, c)
+    assert ops.refine_launches(n, rows, c, small) > ops.refine_launches(n, rows, c)
+    whole = ops.refine(bank, rows, c, p, 0, rows, n - 1, k1, m2)
+    rounds = ops.refine(bank, rows, c, p, 0, rows, n - 1, k1, m2, workspace_bytes=small)
+    assert torch.equal(whole, rounds)
+    got = ops.trimmed_mean(rounds, 0, n - 1).view(n, p).cpu().numpy()
     want = omsm.msm(z.numpy(), 0, n - 1)
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=2e-3)   # near-zero distances: see above
+    with pytest.raises(ValueError):
+        ops.refine(bank, rows, c, p, 0, rows, n - 1, k1, m2, workspace_bytes=small - 1024)
     assert _lib_device_error_clear()
 
 
