@@ -344,7 +344,8 @@ def run_b200(args):
     # our kernels per call: lnamd = statistics + stencil; nearest_pool = fill + GEMM; screen_pool = GEMM
     # (its fills are memsets); refine = image bounds + refinement + 3 per fallback round (plan, gather,
     # gathered GEMM), counted by the library
-    per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'prep_bank': 1, 'nearest_pool': 2, 'screen_pool': 1,
+    per_call = {'lnamd': 2, 'lnamd_super_fast': 2, 'center_stats': 2, 'prep_bank': 1, 'nearest_pool': 2,
+                'screen_pool': 1,
                 'refine': 6, 'trimmed_mean': 1, 'score_maps': 1}
     gemm_ops = ('nearest_pool', 'screen_pool')
 

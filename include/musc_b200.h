@@ -46,7 +46,7 @@ enum musc_b200_status {
 
 enum musc_b200_dtype { MUSC_B200_F32 = 0, MUSC_B200_F16 = 1, MUSC_B200_BF16 = 2 };
 
-/* ABI version of this header (bumped on any signature change): 2. */
+/* ABI version of this header (bumped on any signature change): 3. */
 int musc_b200_abi_version(void);
 
 /* Thread-local message of the last failing call on this thread ("" if none). */
@@ -151,9 +151,34 @@ size_t musc_b200_bank_bytes(long long rows, int channels);
  * into the bank of the concatenated rows. */
 int musc_b200_bank_layout(long long rows, int channels, size_t* plane_offsets);
 
-/* z: [rows][channels] fp32, channels % 8 == 0.  bank: >= bank_bytes. */
+/* z: [rows][channels] fp32, channels % 8 == 0.  bank: >= bank_bytes.  The bank
+ * holds z itself (no centring). */
 int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
                         size_t bank_bytes, musc_b200_stream stream);
+
+/* Centring statistics of z [rows][channels] fp32 (rows >= 0) into
+ * stats[channels + 1] fp64: the column sums, then the smallest squared row norm
+ * (+inf for no rows), in a fixed order (the same rows give the same statistics
+ * bit for bit).  workspace: musc_b200_center_stats_bytes(channels) bytes,
+ * 16-byte aligned.  channels <= 6400. */
+size_t musc_b200_center_stats_bytes(int channels);
+int musc_b200_center_stats(const float* z, long long rows, int channels, double* stats, void* workspace,
+                           size_t workspace_bytes, musc_b200_stream stream);
+
+/* prep_bank of the centred rows z - mu, from the statistics of one or more row
+ * blocks (e.g. one per rank) stats[n_parts][channels + 1] and the number of rows
+ * they cover: mu[c] = (sum over the parts of the column sums) / count, applied
+ * only if |mu|^2 <= 4 x the smallest squared row norm of all parts (then
+ * |z - mu| <= 3 |z| for every row; otherwise the bank holds z, as
+ * musc_b200_prep_bank).  Squared distances do not change under a common shift,
+ * and the split's error scales with the row norms, so for clustered rows
+ * (L2-normalised ViT features) centring tightens every bound the screened pass
+ * relies on.  Every bank scored against another (musc_b200_nearest's query and
+ * reference banks, the ranks' blocks of a gathered pool bank) must be prepared
+ * from the same statistics. */
+int musc_b200_prep_bank_centered(const float* z, long long rows, int channels, const double* stats,
+                                 int n_parts, long long count, void* bank, size_t bank_bytes,
+                                 musc_b200_stream stream);
 
 /* Nearest-patch minima, squared: for every query row q (global row
  * query_first_row + q, image (query_first_row + q) / patches_per_image) and
@@ -263,10 +288,11 @@ int musc_b200_refine(const void* bank, long long bank_rows, long long rows, int 
 int musc_b200_trimmed_mean(const float* nearest_sq, long long query_rows, int n_images,
                            int rank_lo, int rank_hi, double* scores, musc_b200_stream stream);
 
-/* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64: bank
- * prep, screened pool pass, refinement to exact minima, interval average
+/* Whole MSM for one bank: z [n][p][c] fp32 -> scores [n][p] float64: column
+ * centring statistics and the centred bank prep, screened pool pass, refinement to exact
+ * minima, interval average
  * (MUSC_B200_MSM_EXACT=1 in the environment: the 3-pass musc_b200_nearest_pool
- * instead of screen + refinement).  The workspace holds the bank and the tables.  n <= 1790 (the
+ * instead of screen + refinement).  The workspace holds the bank, the tables and the statistics.  n <= 1790 (the
  * interval average's shared-memory limit, see musc_b200_trimmed_mean). */
 size_t musc_b200_msm_workspace_bytes(int n, int p, int c);
 

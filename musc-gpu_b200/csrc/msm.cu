@@ -4,10 +4,14 @@
 // reference GPU driver models/modules/_MSM_gpu.py:701-830.
 //
 // Pipeline for one (layer, radius) bank z[N*P][C] fp32:
-//   1. prep_bank_kernel: per row, a power-of-two scale 2^k putting max|z|
-//      in [2^14, 2^15), the split z*2^k = hi + lo with hi = fp16(z*2^k) and
-//      lo = fp16(z*2^k - hi) (together ~22 significant bits, fp32-class
-//      accuracy), the fp32 squared norm (float64 accumulation) and 2^-k.
+//   0. center_partial_kernel / center_finish_kernel: the pool's column sums and
+//      smallest row norm (fixed order), from which mu = the column mean and the
+//      gate |mu| <= 2 min |z|; the bank then holds the centred rows z - mu (same
+//      distances, smaller split-fp16 error).
+//   1. prep_bank_kernel: per row, a power-of-two scale 2^k putting max|z - mu|
+//      in [2^14, 2^15), the split (z - mu)*2^k = hi + lo with hi = fp16(.) and
+//      lo = fp16(. - hi) (together ~22 significant bits, fp32-class accuracy),
+//      the fp32 squared norm (float64 accumulation), 2^-k and the residual norm.
 //   2. nearest_kernel: persistent, warp-specialised tcgen05 GEMM.  Each tile
 //      is 128 query rows x 256 reference rows; per 32-wide K slice TMA brings
 //      A_hi, A_lo, B_hi, B_lo (48 KB) into a 4-deep shared-memory ring, and one
@@ -59,64 +63,171 @@ static BankLayout bank_layout(long long rows, int channels) {
   return {0, plane, 2 * plane, 2 * plane + vec, 2 * plane + 2 * vec, 2 * plane + 3 * vec};
 }
 
+// ------------------------------------------------------------------ centring statistics
+// Centring.  Squared distances are invariant under a common shift of every row, and
+// the error of a split-fp16 dot product scales with |a| |b|, so the bank may hold
+// z - mu with mu the pool's column mean: for features clustered around a common
+// direction (L2-normalised ViT tokens lie in a narrow cone, |z - mu| ~ 0.05-0.4)
+// the screen's error bound shrinks by |a - mu| |b - mu| / (|a| |b|).  The shift is
+// applied only when |mu| <= 2 x the smallest row norm, which keeps |z - mu| <= 3 |z| for
+// every row (a pool mixing rows of very different norms would otherwise lose the
+// small rows' digits to the rounding of z - mu); L2-normalised rows always pass, and so
+// do clusters far from the origin.
+// mu and the gate must be the same for every row of a pool, so they are formed from
+// statistics [C column sums, smallest squared row norm] that the ranks of a multi-GPU
+// pool exchange (each over its own rows).  Everything is evaluated in a fixed order:
+// the same rows give the same statistics, mu and gate bit for bit.
+constexpr int kStatBlocks = 296;  // 2 per SM
+constexpr int kStatWarps = 8;
+
+// Warp w of block b takes rows (b * 8 + w) + k * 8G; lane l owns columns 4l + 128j.  Each
+// warp accumulates its column sums (fp32) in its own shared-memory row and the smallest
+// squared row norm in a register; the block then adds its 8 warp rows in order.
+__global__ void __launch_bounds__(kStatWarps * 32)
+center_partial_kernel(const float* __restrict__ z, long long rows, int channels, float* __restrict__ partial,
+                      float* __restrict__ partial_min) {
+  extern __shared__ float acc[];  // [kStatWarps][channels]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* mine = acc + (size_t)warp * channels;
+  for (int c = lane * 4; c < channels; c += 128) *reinterpret_cast<float4*>(mine + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  float mn = __int_as_float(0x7f800000);
+  for (long long row = (long long)blockIdx.x * kStatWarps + warp; row < rows;
+       row += (long long)gridDim.x * kStatWarps) {
+    const float* zr = z + row * channels;
+    float ss = 0.f;
+    for (int c = lane * 4; c < channels; c += 128) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
+      float4 a = *reinterpret_cast<float4*>(mine + c);
+      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+      *reinterpret_cast<float4*>(mine + c) = a;
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+    mn = fminf(mn, warp_sum(ss));
+  }
+  __shared__ float wmin[kStatWarps];
+  if (lane == 0) wmin[warp] = mn;
+  __syncthreads();
+  for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+    float t = 0.f;
+    for (int w = 0; w < kStatWarps; ++w) t += acc[(size_t)w * channels + c];
+    partial[(size_t)blockIdx.x * channels + c] = t;
+  }
+  if (threadIdx.x == 0) {
+    float m = wmin[0];
+    for (int w = 1; w < kStatWarps; ++w) m = fminf(m, wmin[w]);
+    partial_min[blockIdx.x] = m;
+  }
+}
+
+// stats[c] = the block partials of column c added in block order (fp64); stats[C] = the
+// smallest squared row norm (+inf for no rows), widened by 2^-20 against the fp32
+// accumulation of the norms.
+__global__ void center_finish_kernel(const float* __restrict__ partial, const float* __restrict__ partial_min,
+                                     int blocks, int channels, double* __restrict__ stats) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < channels) {
+    double s = 0.0;
+    for (int b = 0; b < blocks; ++b) s += partial[(size_t)b * channels + c];
+    stats[c] = s;
+  }
+  if (c == 0) {
+    float m = partial_min[0];
+    for (int b = 1; b < blocks; ++b) m = fminf(m, partial_min[b]);
+    stats[channels] = (double)m * (1.0 - 0x1p-20);
+  }
+}
+
 // ------------------------------------------------------------------ prep
 constexpr int kPrepWarps = 8;
+constexpr int kPrepBlocksPerSm = 8;
 
+// Grid-stride over rows, one warp per row.  With `stats` ([n_parts][C + 1] fp64, or null
+// for no centring) each block first forms mu[c] = (sum over the parts of the column sums)
+// / count and the gate |mu|^2 <= 4 x the smallest squared row norm of all parts, both in a
+// fixed order (every block of every rank reaches the same mu and decision); if the gate
+// holds every row is split as (z - mu) 2^k, otherwise as z 2^k.
 __global__ void __launch_bounds__(kPrepWarps * 32)
-prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, __half* __restrict__ hi,
-                 __half* __restrict__ lo, float* __restrict__ norm2, float* __restrict__ inv_scale,
-                 float* __restrict__ lo_norm) {
+prep_bank_kernel(const float* __restrict__ z, long long rows, int channels, const double* __restrict__ stats,
+                 int n_parts, double inv_count, __half* __restrict__ hi, __half* __restrict__ lo,
+                 float* __restrict__ norm2, float* __restrict__ inv_scale, float* __restrict__ lo_norm) {
+  extern __shared__ float mu[];
+  __shared__ double red[kPrepWarps];
+  double mu2 = 0.0;
+  for (int c = threadIdx.x; c < channels; c += blockDim.x) {
+    double s = 0.0;
+    if (stats)
+      for (int p = 0; p < n_parts; ++p) s += stats[(size_t)p * (channels + 1) + c];
+    const float m = (float)(s * inv_count);
+    mu[c] = m;
+    mu2 += (double)m * m;
+  }
+  mu2 = warp_sum(mu2);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mu2;
+  __syncthreads();
+  if (stats) {
+    double t = 0.0, mn = stats[channels];
+    for (int w = 0; w < kPrepWarps; ++w) t += red[w];
+    for (int p = 1; p < n_parts; ++p) mn = fmin(mn, stats[(size_t)p * (channels + 1) + channels]);
+    if (!(t <= 4.0 * mn))  // gate closed: no shift (every thread reaches the same decision)
+      for (int c = threadIdx.x; c < channels; c += blockDim.x) mu[c] = 0.f;
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;  // warp-uniform
-  const float* zr = z + row * channels;
-  float m = 0.f;
-  double ss = 0.0;
-  for (int c = lane * 4; c < channels; c += 128) {
-    float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
-    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-  }
-  m = warp_max(m);
-  ss = warp_sum(ss);
-  int k = 0;
-  if (m > 0.f) {
-    k = 14 - ilogbf(m);
-    k = k > 126 ? 126 : (k < -126 ? -126 : k);
-  }
-  const float s = ldexpf(1.f, k);
-  __half* hr = hi + row * channels;
-  __half* lr = lo + row * channels;
-  double ll = 0.0;
-  for (int c = lane * 4; c < channels; c += 128) {
-    float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
-    const float x[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
-    __half h[4], l[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      h[e] = __float2half_rn(x[e]);
-      l[e] = __float2half_rn(x[e] - __half2float(h[e]));
-      const double le = (double)__half2float(l[e]);
-      ll += le * le;
+  for (long long row = (long long)blockIdx.x * kPrepWarps + (threadIdx.x >> 5); row < rows;
+       row += (long long)gridDim.x * kPrepWarps) {
+    const float* zr = z + row * channels;
+    float m = 0.f;
+    double ss = 0.0;
+    for (int c = lane * 4; c < channels; c += 128) {
+      float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
+      const float4 u = *reinterpret_cast<const float4*>(mu + c);
+      v.x -= u.x; v.y -= u.y; v.z -= u.z; v.w -= u.w;
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
-    uint2 ph, pl;
-    __half2 t;
-    t = __halves2half2(h[0], h[1]); ph.x = *reinterpret_cast<uint32_t*>(&t);
-    t = __halves2half2(h[2], h[3]); ph.y = *reinterpret_cast<uint32_t*>(&t);
-    t = __halves2half2(l[0], l[1]); pl.x = *reinterpret_cast<uint32_t*>(&t);
-    t = __halves2half2(l[2], l[3]); pl.y = *reinterpret_cast<uint32_t*>(&t);
-    *reinterpret_cast<uint2*>(hr + c) = ph;
-    *reinterpret_cast<uint2*>(lr + c) = pl;
-  }
-  ll = warp_sum(ll);
-  if (lane == 0) {
-    norm2[row] = (float)ss;
-    inv_scale[row] = ldexpf(1.f, -k);
-    // Residual norm |z 2^k - hi| in original units, rounded up, for the screen's error
-    // bound: lo carries z 2^k - hi to fp16 rounding (relative 2^-11, absolute 2^-25 for
-    // subnormal lo), so |z 2^k - hi| <= |lo| (1 + 2^-10) + sqrt(C) 2^-24.
-    lo_norm[row] = (float)((sqrt(ll) * (1.0 + 0x1p-10) + sqrt((double)channels) * 0x1p-24) * (1.0 + 1.0e-6)) *
-                   ldexpf(1.f, -k);
+    m = warp_max(m);
+    ss = warp_sum(ss);
+    int k = 0;
+    if (m > 0.f) {
+      k = 14 - ilogbf(m);
+      k = k > 126 ? 126 : (k < -126 ? -126 : k);
+    }
+    const float s = ldexpf(1.f, k);
+    __half* hr = hi + row * channels;
+    __half* lr = lo + row * channels;
+    double ll = 0.0;
+    for (int c = lane * 4; c < channels; c += 128) {
+      float4 v = __ldg(reinterpret_cast<const float4*>(zr + c));
+      const float4 u = *reinterpret_cast<const float4*>(mu + c);
+      v.x -= u.x; v.y -= u.y; v.z -= u.z; v.w -= u.w;
+      const float x[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+      __half h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        h[e] = __float2half_rn(x[e]);
+        l[e] = __float2half_rn(x[e] - __half2float(h[e]));
+        const double le = (double)__half2float(l[e]);
+        ll += le * le;
+      }
+      uint2 ph, pl;
+      __half2 t;
+      t = __halves2half2(h[0], h[1]); ph.x = *reinterpret_cast<uint32_t*>(&t);
+      t = __halves2half2(h[2], h[3]); ph.y = *reinterpret_cast<uint32_t*>(&t);
+      t = __halves2half2(l[0], l[1]); pl.x = *reinterpret_cast<uint32_t*>(&t);
+      t = __halves2half2(l[2], l[3]); pl.y = *reinterpret_cast<uint32_t*>(&t);
+      *reinterpret_cast<uint2*>(hr + c) = ph;
+      *reinterpret_cast<uint2*>(lr + c) = pl;
+    }
+    ll = warp_sum(ll);
+    if (lane == 0) {
+      norm2[row] = (float)ss;
+      inv_scale[row] = ldexpf(1.f, -k);
+      // Residual norm |z 2^k - hi| in original units, rounded up, for the screen's error
+      // bound: lo carries z 2^k - hi to fp16 rounding (relative 2^-11, absolute 2^-25 for
+      // subnormal lo), so |z 2^k - hi| <= |lo| (1 + 2^-10) + sqrt(C) 2^-24.
+      lo_norm[row] = (float)((sqrt(ll) * (1.0 + 0x1p-10) + sqrt((double)channels) * 0x1p-24) * (1.0 + 1.0e-6)) *
+                     ldexpf(1.f, -k);
+    }
   }
 }
 
@@ -538,22 +649,82 @@ extern "C" size_t musc_b200_bank_bytes(long long rows, int channels) {
   return bank_layout(rows, channels).total;
 }
 
-extern "C" int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
-                                   size_t bank_bytes, musc_b200_stream stream) {
+// Workspace of musc_b200_center_stats: fp32 block partials [G][C] and block minima [G].
+extern "C" size_t musc_b200_center_stats_bytes(int channels) {
+  if (channels <= 0) return 0;
+  return align_up((size_t)kStatBlocks * channels * sizeof(float), 256) + kStatBlocks * sizeof(float);
+}
+
+extern "C" int musc_b200_center_stats(const float* z, long long rows, int channels, double* stats, void* workspace,
+                                      size_t workspace_bytes, musc_b200_stream stream) {
+  if (rows < 0 || channels <= 0 || channels % 8 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "center_stats: requires rows >= 0 and channels a positive multiple of 8");
+  if (!stats || !workspace || (rows > 0 && !z)) return fail(MUSC_B200_ERR_INVALID, "center_stats: null pointer");
+  if ((rows > 0 && reinterpret_cast<uintptr_t>(z) % 16 != 0) || reinterpret_cast<uintptr_t>(stats) % 8 != 0 ||
+      reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+    return fail(MUSC_B200_ERR_INVALID, "center_stats: z and workspace must be 16-byte and stats 8-byte aligned");
+  const size_t smem = (size_t)kStatWarps * channels * sizeof(float);
+  if (smem > 200 * 1024) return fail(MUSC_B200_ERR_INVALID, "center_stats: channels above 6400");
+  if (workspace_bytes < musc_b200_center_stats_bytes(channels))
+    return fail(MUSC_B200_ERR_WORKSPACE, "center_stats: workspace smaller than musc_b200_center_stats_bytes");
+  MUSC_TRY(require_sm100());
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(center_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  MUSC_CUDA(attr);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(workspace);
+  float* pmin = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         align_up((size_t)kStatBlocks * channels * sizeof(float), 256));
+  center_partial_kernel<<<kStatBlocks, kStatWarps * 32, smem, s>>>(z, rows, channels, partial, pmin);
+  MUSC_TRY(check_launch("center_partial_kernel"));
+  center_finish_kernel<<<(channels + 255) / 256, 256, 0, s>>>(partial, pmin, kStatBlocks, channels, stats);
+  return check_launch("center_finish_kernel");
+}
+
+static int prep_bank_launch(const float* z, long long rows, int channels, const double* stats, int n_parts,
+                            long long count, void* bank, size_t bank_bytes, cudaStream_t s) {
   MUSC_TRY(check_bank_args(rows, channels));
   if (!z || !bank) return fail(MUSC_B200_ERR_INVALID, "prep_bank: null pointer");
   if (reinterpret_cast<uintptr_t>(z) % 16 != 0 || reinterpret_cast<uintptr_t>(bank) % 1024 != 0)
     return fail(MUSC_B200_ERR_INVALID, "prep_bank: z must be 16-byte and bank 1024-byte aligned");
+  if (stats && (n_parts <= 0 || count <= 0 || reinterpret_cast<uintptr_t>(stats) % 8 != 0))
+    return fail(MUSC_B200_ERR_INVALID, "prep_bank: centring needs n_parts > 0, count > 0 and 8-byte aligned stats");
   const BankLayout l = bank_layout(rows, channels);
   if (bank_bytes < l.total) return fail(MUSC_B200_ERR_WORKSPACE, "prep_bank: bank smaller than musc_b200_bank_bytes");
+  const size_t smem = (size_t)channels * sizeof(float);
+  if (smem > 200 * 1024) return fail(MUSC_B200_ERR_INVALID, "prep_bank: channels above 51200");
   MUSC_TRY(require_sm100());
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(prep_bank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  MUSC_CUDA(attr);
+  const int sms = std::max(1, sm_count());
   uint8_t* b = static_cast<uint8_t*>(bank);
-  const long long blocks = (rows + kPrepWarps - 1) / kPrepWarps;
-  prep_bank_kernel<<<(unsigned)blocks, kPrepWarps * 32, 0, s>>>(
-      z, rows, channels, reinterpret_cast<__half*>(b + l.hi), reinterpret_cast<__half*>(b + l.lo),
+  const long long need = (rows + kPrepWarps - 1) / kPrepWarps;
+  const long long blocks = std::min<long long>(need, (long long)sms * kPrepBlocksPerSm);
+  prep_bank_kernel<<<(unsigned)blocks, kPrepWarps * 32, smem, s>>>(
+      z, rows, channels, stats, stats ? n_parts : 0, stats ? 1.0 / (double)count : 0.0,
+      reinterpret_cast<__half*>(b + l.hi), reinterpret_cast<__half*>(b + l.lo),
       reinterpret_cast<float*>(b + l.norm), reinterpret_cast<float*>(b + l.inv), reinterpret_cast<float*>(b + l.lnorm));
   return check_launch("prep_bank_kernel");
+}
+
+extern "C" int musc_b200_prep_bank(const float* z, long long rows, int channels, void* bank,
+                                   size_t bank_bytes, musc_b200_stream stream) {
+  return prep_bank_launch(z, rows, channels, nullptr, 0, 0, bank, bank_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int musc_b200_prep_bank_centered(const float* z, long long rows, int channels, const double* stats,
+                                            int n_parts, long long count, void* bank, size_t bank_bytes,
+                                            musc_b200_stream stream) {
+  if (!stats) return fail(MUSC_B200_ERR_INVALID, "prep_bank_centered: null stats");
+  return prep_bank_launch(z, rows, channels, stats, n_parts, count, bank, bank_bytes,
+                          reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int musc_b200_nearest(const void* query_bank, long long query_rows, long long query_first_row,
@@ -742,10 +913,15 @@ int msm_bank(const void* bank, int n, int p, int c, int rank_lo, int rank_hi, do
 
 size_t msm_bank_scratch_bytes(int n, int p, int c) { return msm_scratch_bytes(n, p, c); }
 
+// The centring statistics and their workspace, after the bank and the MSM scratch.
+static size_t msm_center_bytes(int c) {
+  return align_up((size_t)(c + 1) * sizeof(double), 1024) + align_up(musc_b200_center_stats_bytes(c), 1024);
+}
+
 extern "C" size_t musc_b200_msm_workspace_bytes(int n, int p, int c) {
   if (n <= 0 || p <= 0 || c <= 0) return 0;
   const long long rows = (long long)n * p;
-  return bank_layout(rows, c).total + msm_scratch_bytes(n, p, c);
+  return bank_layout(rows, c).total + align_up(msm_scratch_bytes(n, p, c), 1024) + msm_center_bytes(c);
 }
 
 extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, int rank_hi, double* scores,
@@ -762,6 +938,10 @@ extern "C" int musc_b200_msm(const float* z, int n, int p, int c, int rank_lo, i
     return fail(MUSC_B200_ERR_INVALID, "msm: workspace must be 1024-byte aligned");
   const size_t bank_size = bank_layout(rows, c).total;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  MUSC_TRY(musc_b200_prep_bank(z, rows, c, ws, bank_size, stream));
+  uint8_t* center = ws + bank_size + align_up(msm_scratch_bytes(n, p, c), 1024);
+  double* stats = reinterpret_cast<double*>(center);
+  uint8_t* partial = center + align_up((size_t)(c + 1) * sizeof(double), 1024);
+  MUSC_TRY(musc_b200_center_stats(z, rows, c, stats, partial, musc_b200_center_stats_bytes(c), stream));
+  MUSC_TRY(musc_b200_prep_bank_centered(z, rows, c, stats, 1, rows, ws, bank_size, stream));
   return msm_bank(ws, n, p, c, rank_lo, rank_hi, scores, ws + bank_size, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -1,8 +1,10 @@
 // Whole-pool scoring on one GPU through the C ABI: the scoring half of
 // MuSc.make_category_data (models/musc.py:224-288) for callers that are not
 // Python -- LNAMD of every hooked layer (all radii in one pass), then per
-// (radius, layer) bank the split-fp16 prep, the symmetric nearest GEMM and the
-// interval average, then the layer/radius means, up-sampling and image maxima.
+// (radius, layer) bank the centring statistics and the centred split-fp16 prep, the
+// screened symmetric pass and its refinement to exact minima (or the 3-pass exact
+// pass, MUSC_B200_MSM_EXACT=1) and the interval average, then the layer/radius
+// means, up-sampling and image maxima.
 // Every launch goes to the caller's stream; scratch lives in one caller
 // workspace sized by musc_b200_score_pool_bytes.
 #include "common.cuh"
@@ -20,7 +22,7 @@ namespace {
 size_t align_1k(size_t v) { return (v + 1023) / 1024 * 1024; }
 
 struct PoolWorkspace {
-  size_t stats, z, bank, table, total;
+  size_t stats, z, bank, table, center, partial, total;
 };
 
 PoolWorkspace pool_layout(int n, int p, int c, int n_radii) {
@@ -30,7 +32,9 @@ PoolWorkspace pool_layout(int n, int p, int c, int n_radii) {
   w.z = align_1k(musc_b200_lnamd_workspace_bytes(n));
   w.bank = w.z + align_1k((size_t)n_radii * rows * c * sizeof(float));
   w.table = w.bank + align_1k(musc_b200_bank_bytes(rows, c));
-  w.total = w.table + align_1k(msm_bank_scratch_bytes(n, p, c));
+  w.center = w.table + align_1k(msm_bank_scratch_bytes(n, p, c));
+  w.partial = w.center + align_1k((size_t)(c + 1) * sizeof(double));
+  w.total = w.partial + align_1k(musc_b200_center_stats_bytes(c));
   return w;
 }
 
@@ -83,7 +87,10 @@ extern "C" int musc_b200_score_pool(const void* const* tokens, int dtype, int n_
     MUSC_TRY(musc_b200_lnamd(tokens[li], dtype, n_images, tokens_per_image, channels, n_radii, radii, outs,
                              (long long)p * channels, channels, 1, ws + w.stats, w.z - w.stats, stream));
     for (int ri = 0; ri < n_radii; ++ri) {
-      MUSC_TRY(musc_b200_prep_bank(outs[ri], rows, channels, ws + w.bank, w.table - w.bank, stream));
+      double* center = reinterpret_cast<double*>(ws + w.center);
+      MUSC_TRY(musc_b200_center_stats(outs[ri], rows, channels, center, ws + w.partial, w.total - w.partial, stream));
+      MUSC_TRY(musc_b200_prep_bank_centered(outs[ri], rows, channels, center, 1, rows, ws + w.bank,
+                                            w.table - w.bank, stream));
       MUSC_TRY(msm_bank(ws + w.bank, n_images, p, channels, a, b, scores + ((size_t)ri * n_layers + li) * rows,
                         ws + w.table, reinterpret_cast<cudaStream_t>(stream)));
     }

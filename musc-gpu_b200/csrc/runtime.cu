@@ -78,7 +78,7 @@ int* device_error_ptr(void) {
 
 }  // namespace musc
 
-extern "C" int musc_b200_abi_version(void) { return 2; }
+extern "C" int musc_b200_abi_version(void) { return 3; }
 
 extern "C" const char* musc_b200_last_error(void) { return musc::g_last_error.c_str(); }
 

@@ -35,6 +35,9 @@ SIGNATURES = {
                                           _vp, _sz, _vp]),
     'musc_b200_bank_bytes': (_sz, [_ll, _int]),
     'musc_b200_prep_bank': (_int, [_vp, _ll, _int, _vp, _sz, _vp]),
+    'musc_b200_center_stats_bytes': (_sz, [_int]),
+    'musc_b200_center_stats': (_int, [_vp, _ll, _int, _vp, _vp, _sz, _vp]),
+    'musc_b200_prep_bank_centered': (_int, [_vp, _ll, _int, _vp, _int, _ll, _vp, _sz, _vp]),
     'musc_b200_nearest': (_int, [_vp, _ll, _ll, _vp, _ll, _int, _int, _vp, _vp]),
     'musc_b200_nearest_pool_bytes': (_sz, [_ll, _int, _ll]),
     'musc_b200_nearest_pool': (_int, [_vp, _ll, _ll, _int, _int, _int, _int, _ll, _int, _vp, _vp]),

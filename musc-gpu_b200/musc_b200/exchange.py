@@ -1,7 +1,10 @@
 """Copy-engine transport of the multi-GPU pool scoring (one process per GPU, one node).
 
-``pipeline.score_pool`` exchanges two things per bank between the ranks:
+``pipeline.score_pool`` exchanges three things per bank between the ranks:
 
+* the centring statistics of every rank's rows (column sums, smallest row norm), so
+  that every rank centres its bank rows on the same pool mean before the split (a few
+  KB, copied on the compute stream);
 * the bank planes: every rank preps the bank of its own query images and needs the
   whole pool's bank (an all-gather);
 * the screen tables: every rank screens its share of the symmetric tiles into tables
@@ -18,9 +21,10 @@ awaited with stream-ordered waits on one's own flags, so no host synchronisation
 SM time is involved.  A mapped peer pointer is only ever a copy source: no kernel and no
 library routine reads a peer's memory.
 
-Flags of rank r (``[world][4]`` uint32, written by the peers, row = the writer):
+Flags of rank r (``[world][6]`` uint32, written by the peers, row = the writer):
 ``BANK_READY`` (the writer's bank k is prepared), ``BANK_TAKEN`` (the writer has copied
-r's bank k, so r may reuse the buffer), ``SCREEN_READY``, ``SCREEN_TAKEN``.  The value is
+r's bank k, so r may reuse the buffer), ``SCREEN_READY``, ``SCREEN_TAKEN``,
+``SUMS_READY``, ``SUMS_TAKEN`` (the same for the centring statistics).  The value is
 the exchange's bank counter, which only grows (across calls too), so a wait for
 ``>= v`` never confuses banks.
 """
@@ -32,7 +36,9 @@ import torch
 
 from . import _lib, ops
 
-BANK_READY, BANK_TAKEN, SCREEN_READY, SCREEN_TAKEN = range(4)
+BANK_READY, BANK_TAKEN, SCREEN_READY, SCREEN_TAKEN, SUMS_READY, SUMS_TAKEN = range(6)
+N_FLAGS = 6
+FLAGS_SLOT, STATS_SLOT = 6, 7   # positions of the flags and of stats[0] among the shared buffers
 
 
 def _vp(x: int) -> ctypes.c_void_p:
@@ -62,9 +68,12 @@ class PeerExchange:
             self.local_bank = [ops.empty_bank(self.local_rows, channels, dev) for _ in range(2)]
             self.screens = [ops.screen_table(self.rows, patches, self.rpb, dev, min_blocks=self.world)
                             for _ in range(2)]
-            self.flags = torch.zeros(self.world, 4, dtype=torch.int32, device=dev)
+            self.flags = torch.zeros(self.world, N_FLAGS, dtype=torch.int32, device=dev)
+            self.stats = [torch.zeros(channels + 1, dtype=torch.float64, device=dev) for _ in range(2)]
             # filled by this rank's copies
             self.full_bank = [ops.empty_bank(self.bank_rows, channels, dev) for _ in range(3)]
+            self.stats_all = [torch.empty(self.world, channels + 1, dtype=torch.float64, device=dev)
+                              for _ in range(2)]
             self.recv = [(torch.empty(self.world, n_images, self.rpb, dtype=torch.int64, device=dev),
                           torch.empty(self.world, n_images, self.rpb, dtype=torch.int32, device=dev))
                          for _ in range(2)]
@@ -72,7 +81,7 @@ class PeerExchange:
             torch.cuda.synchronize(dev)
         # IPC handles of the buffers the peers read, exchanged once
         shared = [self.local_bank[0], self.local_bank[1], self.screens[0][0], self.screens[0][1],
-                  self.screens[1][0], self.screens[1][1], self.flags]
+                  self.screens[1][0], self.screens[1][1], self.flags, self.stats[0], self.stats[1]]
         mine = []
         for t in shared:
             h = (ctypes.c_ubyte * 64)()
@@ -115,11 +124,11 @@ class PeerExchange:
 
     # ------------------------------------------------------------------ flag helpers
     def _my_flag(self, writer: int, kind: int) -> ctypes.c_void_p:
-        return _vp(self.flags.data_ptr() + (writer * 4 + kind) * 4)
+        return _vp(self.flags.data_ptr() + (writer * N_FLAGS + kind) * 4)
 
     def _peer_flag(self, peer: int, kind: int) -> ctypes.c_void_p:
         # this rank's row in the peer's flags
-        return _vp(self.peer[peer][6] + (self.rank * 4 + kind) * 4)
+        return _vp(self.peer[peer][FLAGS_SLOT] + (self.rank * N_FLAGS + kind) * 4)
 
     def _signal_peers(self, kind: int, value: int, stream) -> None:
         lib = _lib.lib()
@@ -143,6 +152,31 @@ class PeerExchange:
         """Counter value of the next bank (1, 2, ...)."""
         self.counter += 1
         return self.counter
+
+    def center(self, v: int, compute, z_local: torch.Tensor, kernels) -> torch.Tensor:
+        """Centring statistics of bank ``v``: this rank reduces its rows ``z_local`` on
+        ``compute``, signals the peers and copies every rank's statistics (the compute stream
+        waits for each peer's).  Returns the ``(world, C + 1)`` fp64 statistics for the
+        centred prep."""
+        if v > 2:
+            for s in self.peer:
+                self._wait(s, SUMS_TAKEN, v - 2, compute)
+        mine = self.stats[v % 2]
+        kernels.center_stats(z_local, out=mine)
+        self._signal_peers(SUMS_READY, v, compute)
+        out = self.stats_all[v % 2]
+        nb = (self.c + 1) * 8
+        for s in range(self.world):
+            if s == self.rank:
+                src = mine.data_ptr()
+            else:
+                self._wait(s, SUMS_READY, v, compute)
+                src = self.peer[s][STATS_SLOT + v % 2]
+            self._copy(out.data_ptr() + s * nb, src, nb, compute)
+            if s != self.rank:
+                _lib.check(_lib.lib().musc_b200_stream_signal(self._peer_flag(s, SUMS_TAKEN), v,
+                                                              _vp(compute.cuda_stream)), 'musc_b200_stream_signal')
+        return out
 
     def local_bank_for(self, v: int, compute) -> torch.Tensor:
         """This rank's bank buffer for bank ``v``, once every peer has copied bank ``v - 2``

@@ -155,8 +155,38 @@ def trimmed_ranks(n_images: int, topmin_min: float = 0, topmin_max: float = 0.3)
     return a, b
 
 
-def prep_bank(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Split-fp16 tensor-core operand bank of ``z`` ``(rows, C)`` fp32."""
+def center_stats(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Centring statistics of ``z`` ``(rows, C)`` fp32: fp64 ``(C + 1,)`` = the column sums
+    and the smallest squared row norm, in a fixed order (the input of :func:`prep_bank`; a
+    rank of a multi-GPU pool takes them over its own rows)."""
+    _require_cuda(z, 'center_stats')
+    if z.ndim != 2 or z.dtype != torch.float32:
+        raise ValueError('center_stats: expected (rows, C) float32')
+    z = z.contiguous()
+    rows, c = z.shape
+    dev = z.device
+    if out is None:
+        out = torch.empty(c + 1, dtype=torch.float64, device=dev)
+    if out.dtype != torch.float64 or out.numel() != c + 1 or not out.is_contiguous():
+        raise ValueError('center_stats: out must be a contiguous float64 tensor of C + 1 elements')
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        nbytes = lib.musc_b200_center_stats_bytes(c)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _lib.check(lib.musc_b200_center_stats(_ptr(z) if rows else None, rows, c, _ptr(out), _ptr(ws), nbytes,
+                                              _stream(dev)), 'musc_b200_center_stats')
+    return out
+
+
+def prep_bank(z: torch.Tensor, out: torch.Tensor | None = None, stats: torch.Tensor | None = None,
+              count: int | None = None) -> torch.Tensor:
+    """Split-fp16 tensor-core operand bank of ``z`` ``(rows, C)`` fp32.
+
+    With ``stats`` (fp64 ``(C + 1,)`` or ``(parts, C + 1)`` from :func:`center_stats`, one
+    row per block of the pool) the bank holds the centred rows ``z - mu``,
+    ``mu = column sums / count`` (``count`` defaults to ``rows``), when
+    ``|mu| <= 2 min |z|`` over the pool; every bank scored against this one must be
+    prepared from the same statistics."""
     _require_cuda(z, 'prep_bank')
     if z.ndim != 2 or z.dtype != torch.float32:
         raise ValueError('prep_bank: expected (rows, C) float32')
@@ -167,8 +197,18 @@ def prep_bank(z: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         lib = _lib.lib()
         nbytes = lib.musc_b200_bank_bytes(rows, c)
         bank = _aligned_empty(nbytes, dev) if out is None else out
-        _lib.check(lib.musc_b200_prep_bank(_ptr(z), rows, c, _ptr(bank), nbytes, _stream(dev)),
-                   'musc_b200_prep_bank')
+        if stats is None:
+            _lib.check(lib.musc_b200_prep_bank(_ptr(z), rows, c, _ptr(bank), nbytes, _stream(dev)),
+                       'musc_b200_prep_bank')
+        else:
+            if (stats.dtype != torch.float64 or stats.shape[-1] != c + 1 or not stats.is_contiguous()
+                    or stats.device != dev):
+                raise ValueError('prep_bank: stats must be contiguous float64 (C + 1,) or (parts, C + 1) '
+                                 'on the device')
+            parts = 1 if stats.ndim == 1 else stats.shape[0]
+            _lib.check(lib.musc_b200_prep_bank_centered(_ptr(z), rows, c, _ptr(stats), parts,
+                                                        rows if count is None else int(count), _ptr(bank),
+                                                        nbytes, _stream(dev)), 'musc_b200_prep_bank_centered')
     return bank
 
 

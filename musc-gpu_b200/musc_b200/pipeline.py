@@ -6,7 +6,8 @@ This is the scoring half of ``MuSc.make_category_data``
 * per layer, one LNAMD launch produces the L2-normalised banks of all radii
   (``models/musc.py:227-245``; the bank assembly ``Z = cat(Z_layers[l])`` of
   ``:252`` is the output layout itself);
-* per (radius, layer) bank, MSM (``:248-262``) = bank prep, the fused
+* per (radius, layer) bank, MSM (``:248-262``) = the bank prep (centred on the
+  pool's column mean: same distances, tighter split-fp16 bounds), the fused
   distance/min GEMM and the interval average;
 * layer and radius means, up-sampling and image maxima (``:259-288``).
 
@@ -162,6 +163,7 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
     exact_path = exact_pool_path()
     if world == 1:
         bank = kernels.empty_bank(rows, c, dev)
+        stats = torch.empty(c + 1, dtype=torch.float64, device=dev)
         if exact_path:
             table = kernels.nearest_pool_table(rows, p, rows, dev)
         else:
@@ -169,7 +171,8 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
             table = torch.empty(1, n_images, rows, dtype=torch.float32, device=dev)
         for li, ri in banks:
             aggregate(li)
-            kernels.prep_bank(local[ri, :n_images].reshape(rows, c), out=bank)
+            z = local[ri, :n_images].reshape(rows, c)
+            kernels.prep_bank(z, out=bank, stats=kernels.center_stats(z, out=stats), count=rows)
             if exact_path:
                 kernels.nearest_pool(bank, rows, c, p, 0, 1, rows, out=table)
             else:
@@ -190,11 +193,18 @@ def score_pool(tokens: Sequence[torch.Tensor], n_images: int | None = None,
         gather_group = _side_group(group)
         local_bank = [kernels.empty_bank(local_rows, c, dev) for _ in range(2)]
         full_bank = [kernels.empty_bank(bank_rows, c, dev) for _ in range(3)]
+        stats_local = [torch.empty(c + 1, dtype=torch.float64, device=dev) for _ in range(2)]
+        stats_all = [torch.empty(world, c + 1, dtype=torch.float64, device=dev) for _ in range(2)]
 
         def start_gather(k):
             li, ri = banks[k]
             aggregate(li)
-            kernels.prep_bank(local[ri].reshape(local_rows, c), out=local_bank[k % 2])
+            # every rank centres on the same mean: the ranks' statistics (over their real
+            # rows, not the padding), gathered
+            kernels.center_stats(local[ri, :n_local].reshape(-1, c), out=stats_local[k % 2])
+            dist.all_gather_into_tensor(stats_all[k % 2].view(-1), stats_local[k % 2], group=gather_group)
+            kernels.prep_bank(local[ri].reshape(local_rows, c), out=local_bank[k % 2], stats=stats_all[k % 2],
+                              count=rows)
             pieces = zip(kernels.bank_planes(full_bank[k % 3], bank_rows, c),
                          kernels.bank_planes(local_bank[k % 2], local_rows, c))
             return [dist.all_gather_into_tensor(f, l, group=gather_group, async_op=True) for f, l in pieces]
@@ -282,8 +292,9 @@ def _score_with_exchange(kernels, ex, banks, aggregate, local, select, rows, c, 
         li, ri = banks[k]
         aggregate(li)
         v = ex.begin_bank()
+        stats = ex.center(v, compute, local[ri].reshape(ex.local_rows, c)[:q_rows], kernels)
         lb = ex.local_bank_for(v, compute)
-        kernels.prep_bank(local[ri].reshape(ex.local_rows, c), out=lb)
+        kernels.prep_bank(local[ri].reshape(ex.local_rows, c), out=lb, stats=stats, count=rows)
         full, events = ex.gather(v, compute)
         return v, k, full, events
 

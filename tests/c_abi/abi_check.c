@@ -18,7 +18,7 @@ static void expect(int cond, const char* what) {
 }
 
 int main(void) {
-  expect(musc_b200_abi_version() == 2, "abi version");
+  expect(musc_b200_abi_version() == 3, "abi version");
   expect(musc_b200_lnamd_workspace_bytes(4) == 4 * 8 * 2 * sizeof(double), "lnamd workspace");
   expect(musc_b200_bank_bytes(1369, 1024) % 1024 == 0, "bank bytes aligned");
   expect(musc_b200_nearest_pool_bytes(16 * 1369, 1369, 16 * 1369) >= (size_t)16 * 16 * 1369 * 4,

@@ -55,7 +55,24 @@ class OracleKernels:
         return [bank[:rows].reshape(-1)]
 
     @staticmethod
-    def prep_bank(z, out=None):
+    def center_stats(z, out=None):
+        x = z.numpy().astype(np.float64)
+        norms = (z.numpy() ** 2).sum(1)
+        s = np.concatenate([x.sum(0), [norms.min() * (1 - 2 ** -20) if len(norms) else np.inf]])
+        if out is None:
+            return torch.from_numpy(s)
+        out.copy_(torch.from_numpy(s))
+        return out
+
+    @staticmethod
+    def prep_bank(z, out=None, stats=None, count=None):
+        # the library's centring: fp32 mu from the fp64 sums of every part, applied when
+        # |mu|^2 <= 4 x the smallest squared row norm of every part
+        if stats is not None:
+            st = stats.reshape(-1, z.shape[1] + 1)
+            mu = (st[:, :-1].sum(0) / (z.shape[0] if count is None else count)).float()
+            if float((mu.double() ** 2).sum()) <= 4 * float(st[:, -1].min()):
+                z = z - mu
         if out is None:
             return z.clone()
         out[:z.shape[0]].copy_(z)

@@ -532,3 +532,88 @@ def test_msm_screen_path_equals_exact_path_config2_bank(cuda_device, monkeypatch
     exact = ops.msm(z)
     torch.testing.assert_close(deferred, exact, rtol=2e-6, atol=0)
     assert _lib_device_error_clear()
+
+
+@pytest.mark.parametrize('rows,c', [(0, 64), (1, 8), (1000, 1024), (37 * 296 + 5, 2048)])
+def test_center_stats_in_a_fixed_order(cuda_device, rows, c):
+    """The centring statistics: column sums (fp32 partials added in fp64) and the smallest
+    squared row norm, the same bits on every call; zeros and +inf for an empty block."""
+    from musc_b200 import ops
+    z = torch.randn(rows, c, generator=torch.Generator().manual_seed(rows + c)).to(cuda_device)
+    s1 = ops.center_stats(z)
+    s2 = ops.center_stats(z)
+    assert torch.equal(s1, s2)
+    torch.testing.assert_close(s1[:c], z.double().sum(0), rtol=1e-6, atol=1e-6 * max(rows, 1) ** 0.5)
+    if rows:
+        want = (z.double() ** 2).sum(1).min()
+        assert want * (1 - 2e-6) <= s1[c] <= want
+    else:
+        assert torch.isinf(s1[c])
+    assert _lib_device_error_clear()
+
+
+@pytest.mark.parametrize('n,p,c,shift', [(12, 196, 256, 0.0), (6, 784, 512, 0.0), (9, 196, 256, 3.0)])
+def test_centred_msm_on_clustered_features(cuda_device, n, p, c, shift):
+    """Features in a narrow cone, |z - mu| ~ 0.1 as for ViT tokens (without centring the
+    screen's bound, ~1e-3 for unit rows, exceeds most nearest-neighbour gaps there): the
+    screened + refined MSM equals MSM over float64 distances.  A pool shifted by a constant
+    vector (|z| ~ 3.2) scores the same: the centring removes the shift, where fp32
+    |a|^2 + |b|^2 - 2 a.b over the shifted rows would lose ~1e-3 to cancellation."""
+    from musc_b200 import ops
+    g = torch.Generator().manual_seed(n * 13 + c)
+    d = torch.randn(c, generator=g)
+    z = d / d.norm() + (0.1 / c ** 0.5) * torch.randn(n, p, c, generator=g)
+    z = z / z.norm(dim=-1, keepdim=True)
+    if shift:
+        z = z + shift * torch.ones(c) / c ** 0.5
+    got = ops.msm(z.to(cuda_device)).cpu().numpy()
+    np.testing.assert_allclose(got, _msm_float64(z.numpy()), rtol=RTOL, atol=0)
+    assert _lib_device_error_clear()
+
+
+def _msm_float64(z: np.ndarray, topmin_max: float = 0.3) -> np.ndarray:
+    """MSM with float64 distances of the fp32 rows (the reference's fp32 |q|^2 + |p|^2 - 2 q.p
+    loses ~1e-7 (|q|^2 + |p|^2) to cancellation, more than the tolerance for rows of norm 3)."""
+    n, p, c = z.shape
+    flat = z.reshape(n * p, c).astype(np.float64)
+    a, b = omsm.trimmed_ranks(n, 0, topmin_max)
+    out = []
+    for i in range(n):
+        q = flat[i * p:(i + 1) * p]
+        d2 = (q * q).sum(1)[:, None] + (flat * flat).sum(1)[None, :] - 2.0 * (q @ flat.T)
+        minima = np.sqrt(np.maximum(d2.reshape(p, n, p).min(axis=2), 0.0))[:, [j for j in range(n) if j != i]]
+        out.append(omsm.interval_average(minima, a, b))
+    return np.stack(out)
+
+
+def test_centred_banks_share_one_mean(cuda_device):
+    """A pool split into row blocks (the ranks of a multi-GPU pool), each block prepared
+    with the gathered statistics of all blocks, is bit for bit the bank of the whole pool
+    prepared with the same statistics (and differs from the uncentred bank); and the screen + refinement of a centred bank equals the 3-pass
+    exact table of the uncentred one within fp32 rounding (distances do not move)."""
+    from musc_b200 import ops
+    n, p, c = 8, 196, 128
+    g = torch.Generator().manual_seed(77)
+    d = torch.randn(c, generator=g)
+    z = (d / d.norm() + (0.1 / c ** 0.5) * torch.randn(n * p, c, generator=g)).to(cuda_device)
+    z = z / z.norm(dim=-1, keepdim=True)
+    rows = n * p
+    blocks = [z[:3 * p], z[3 * p:6 * p], z[6 * p:]]
+    stats = torch.stack([ops.center_stats(b) for b in blocks])
+    whole = ops.prep_bank(z, stats=stats, count=rows)
+    parts = [ops.prep_bank(b, stats=stats, count=rows) for b in blocks]
+    wp = ops.bank_planes(whole, rows, c)
+    pp = [ops.bank_planes(bk, blk.shape[0], c) for bk, blk in zip(parts, blocks)]
+    for i in range(5):
+        assert torch.equal(wp[i], torch.cat([q[i] for q in pp]))
+    assert not torch.equal(wp[0], ops.bank_planes(ops.prep_bank(z), rows, c)[0])
+    k1, m2, _ = ops.screen_pool(whole, rows, c, p)
+    b = int((n - 1) * 0.3)
+    ref = ops.refine(whole, rows, c, p, 0, rows, b, k1, m2).cpu().numpy()
+    flat = z.cpu().numpy().astype(np.float64)
+    d2 = (flat * flat).sum(1)[:, None] + (flat * flat).sum(1)[None, :] - 2.0 * (flat @ flat.T)
+    want = d2.reshape(rows, n, p).min(axis=2).T                          # (n, rows) float64 squared minima
+    kept = ref != np.finfo(np.float32).max
+    assert kept.sum() >= rows * b
+    np.testing.assert_allclose(ref[kept], want[kept], rtol=2e-5, atol=1e-7)
+    assert _lib_device_error_clear()

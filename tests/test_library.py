@@ -37,7 +37,7 @@ def test_host_only_queries():
     """Size queries and argument validation run without a device."""
     from musc_b200 import _lib
     lib = _lib.lib()
-    assert lib.musc_b200_abi_version() == 2
+    assert lib.musc_b200_abi_version() == 3
     assert lib.musc_b200_lnamd_workspace_bytes(0) == 0
     assert lib.musc_b200_lnamd_workspace_bytes(4) == 4 * 8 * 2 * 8
     assert lib.musc_b200_bank_bytes(1369, 1024) >= 1369 * 1024 * 4
