@@ -54,7 +54,8 @@ namespace {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-constexpr int kRefineThreads = 256;  // 8 warps
+constexpr int kRefineThreads = 256;     // 8 warps, one per row
+constexpr int kRefineMaxThreads = 512;  // large pools: 16 warps, two per row
 
 struct BankPlanes {
   const __half* hi;
@@ -174,6 +175,7 @@ struct RefineParams {
   int* lists;                    // [n_images][q_rows] queued local rows
   int rows_per_cta;
   int pitch;                     // smem row pitch (>= n_images)
+  int warps_per_row;             // warps sharing a row's exact evaluations (1 or 2)
 };
 
 __device__ __forceinline__ float key_value(unsigned long long k) {
@@ -250,14 +252,14 @@ __device__ void exact_d2_pair(const BankPlanes& b, long long qa, long long p0, l
   *d1 = warp_sum(a1);
 }
 
-__global__ void __launch_bounds__(kRefineThreads)
+__global__ void __launch_bounds__(kRefineMaxThreads)
 refine_kernel(const RefineParams rp) {
   extern __shared__ uint8_t smem_raw[];
   // [rows_per_cta][pitch] combined keys, second minima and the output row.
   unsigned long long* sk = reinterpret_cast<unsigned long long*>(smem_raw);
   uint32_t* sm2 = reinterpret_cast<uint32_t*>(sk + (size_t)rp.rows_per_cta * rp.pitch);
   float* sx = reinterpret_cast<float*>(sm2 + (size_t)rp.rows_per_cta * rp.pitch);
-  float* su = sx + (size_t)rp.rows_per_cta * rp.pitch;  // per-warp scratch [8][pitch]: upper bounds
+  float* su = sx + (size_t)rp.rows_per_cta * rp.pitch;  // per-warp scratch [warps][pitch]: upper bounds
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long r0 = (long long)blockIdx.x * rp.rows_per_cta;
   const int R = rp.rows_per_cta, N = rp.n_images;
@@ -286,10 +288,13 @@ refine_kernel(const RefineParams rp) {
   }
   __syncthreads();
 
-  // 2. One warp per row.
+  // 2. One warp per row, or (large pools, few rows per CTA) `warps_per_row` warps: each
+  // forms the row's bounds and threshold and evaluates every warps_per_row-th block of 32
+  // images, so twice the row gathers are in flight per SM.
   float* u = su + (size_t)warp * rp.pitch;
   const float lo_scale = 1.f - 6.2e-5f, hi_scale = 1.f + 6.2e-5f;  // 2^-14 on either side
-  for (int r = warp; r < R; r += kRefineThreads / 32) {
+  const int wpr = rp.warps_per_row, sub = warp % wpr;
+  for (int r = warp / wpr; r < R; r += (int)(blockDim.x >> 5) / wpr) {
     const long long q = r0 + r;
     if (q >= rp.q_rows) break;  // warp-uniform
     const long long grow = rp.first_row + q;
@@ -327,7 +332,7 @@ refine_kernel(const RefineParams rp) {
     const float T = __uint_as_float(lo);
     // Per image: excluded (FLT_MAX), certified exact, or an upper bound queued for the
     // exact fallback.
-    for (int jb = 0; jb < N; jb += 32) {
+    for (int jb = sub * 32; jb < N; jb += 32 * wpr) {
       const int j = jb + lane;
       bool need = false;
       float lower = 0.f, e = 0.f;
@@ -453,16 +458,21 @@ fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const
   }
 }
 
-int refine_rows_per_cta(int n_images, int* pitch, size_t* smem) {
+// Rows per CTA, threads and warps per row: 32 rows of 8 one-row warps while they fit in
+// shared memory; when fewer rows fit (large pools), 16 warps, two per row.
+int refine_rows_per_cta(int n_images, int* pitch, size_t* smem, int* threads, int* wpr) {
   int rows = 32;
   const int pt = n_images + ((2 - n_images % 2) % 2);  // even, so the 8-byte keys stay aligned
-  while (rows > 1) {
-    const size_t bytes = (size_t)rows * pt * (8 + 4 + 4) + (size_t)(kRefineThreads / 32) * pt * 4;
-    if ((long long)bytes <= smem_optin() - 4096) break;
-    rows >>= 1;
+  auto bytes_for = [&](int r, int warps) { return (size_t)r * pt * (8 + 4 + 4) + (size_t)warps * pt * 4; };
+  while (rows > 1 && (long long)bytes_for(rows, kRefineThreads / 32) > smem_optin() - 4096) rows >>= 1;
+  *threads = kRefineThreads;
+  *wpr = 1;
+  if (rows < 32 && (long long)bytes_for(rows, kRefineMaxThreads / 32) <= smem_optin() - 4096) {
+    *threads = kRefineMaxThreads;
+    *wpr = 2;
   }
   *pitch = pt;
-  *smem = (size_t)rows * pt * (8 + 4 + 4) + (size_t)(kRefineThreads / 32) * pt * 4;
+  *smem = bytes_for(rows, *threads / 32);
   return rows;
 }
 
@@ -534,12 +544,13 @@ int refine_launch(const void* bank, long long bank_rows, long long rows, int cha
   rp.counts = counts;
   rp.lists = lists;
   size_t smem = 0;
-  rp.rows_per_cta = refine_rows_per_cta(n_images, &rp.pitch, &smem);
+  int threads = kRefineThreads;
+  rp.rows_per_cta = refine_rows_per_cta(n_images, &rp.pitch, &smem, &threads, &rp.warps_per_row);
   if (rp.rows_per_cta < 1 || (long long)smem > smem_optin())
     return fail(MUSC_B200_ERR_INVALID, "refine: too many images for the refinement's shared memory");
   MUSC_CUDA(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const long long blocks = (q_rows + rp.rows_per_cta - 1) / rp.rows_per_cta;
-  refine_kernel<<<(unsigned)blocks, kRefineThreads, smem, s>>>(rp);
+  refine_kernel<<<(unsigned)blocks, (unsigned)threads, smem, s>>>(rp);
   MUSC_TRY(check_launch("refine_kernel"));
 
   // Exact 3-pass evaluation of the queued rows against their images, in rounds of at
