@@ -55,7 +55,7 @@ namespace {
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 constexpr int kRefineThreads = 256;     // 8 warps, one per row
-constexpr int kRefineMaxThreads = 512;  // large pools: 16 warps, two per row
+constexpr int kRefineMaxThreads = 768;  // large pools: 24 warps sharing fewer rows
 
 struct BankPlanes {
   const __half* hi;
@@ -175,7 +175,7 @@ struct RefineParams {
   int* lists;                    // [n_images][q_rows] queued local rows
   int rows_per_cta;
   int pitch;                     // smem row pitch (>= n_images)
-  int warps_per_row;             // warps sharing a row's exact evaluations (1 or 2)
+  int warps_per_row;             // warps sharing a row's bounds and exact evaluations
 };
 
 __device__ __forceinline__ float key_value(unsigned long long k) {
@@ -259,7 +259,7 @@ refine_kernel(const RefineParams rp) {
   unsigned long long* sk = reinterpret_cast<unsigned long long*>(smem_raw);
   uint32_t* sm2 = reinterpret_cast<uint32_t*>(sk + (size_t)rp.rows_per_cta * rp.pitch);
   float* sx = reinterpret_cast<float*>(sm2 + (size_t)rp.rows_per_cta * rp.pitch);
-  float* su = sx + (size_t)rp.rows_per_cta * rp.pitch;  // per-warp scratch [warps][pitch]: upper bounds
+  float* su = sx + (size_t)rp.rows_per_cta * rp.pitch;  // per-group scratch [groups][pitch]: upper bounds
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long r0 = (long long)blockIdx.x * rp.rows_per_cta;
   const int R = rp.rows_per_cta, N = rp.n_images;
@@ -288,13 +288,18 @@ refine_kernel(const RefineParams rp) {
   }
   __syncthreads();
 
-  // 2. One warp per row, or (large pools, few rows per CTA) `warps_per_row` warps: each
-  // forms the row's bounds and threshold and evaluates every warps_per_row-th block of 32
-  // images, so twice the row gathers are in flight per SM.
-  float* u = su + (size_t)warp * rp.pitch;
+  // 2. One warp per row, or (large pools, few rows per CTA) a group of `warps_per_row`
+  // warps per row: the group fills the row's upper bounds together (every wpr-th block of
+  // 32 images per warp, one shared array, a named barrier per group), each warp finds the
+  // threshold, and each evaluates its own blocks -- more row gathers in flight per SM.
+  const int wpr = rp.warps_per_row, sub = warp % wpr, group = warp / wpr;
+  float* u = su + (size_t)group * rp.pitch;
   const float lo_scale = 1.f - 6.2e-5f, hi_scale = 1.f + 6.2e-5f;  // 2^-14 on either side
-  const int wpr = rp.warps_per_row, sub = warp % wpr;
-  for (int r = warp / wpr; r < R; r += (int)(blockDim.x >> 5) / wpr) {
+  auto group_sync = [&]() {
+    if (wpr == 1) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(32 * wpr) : "memory");
+  };
+  for (int r = group; r < R; r += (int)(blockDim.x >> 5) / wpr) {
     const long long q = r0 + r;
     if (q >= rp.q_rows) break;  // warp-uniform
     const long long grow = rp.first_row + q;
@@ -312,13 +317,14 @@ refine_kernel(const RefineParams rp) {
       return e * (1.f + 1.0e-5f);
     };
     // upper bounds U_j (FLT_MAX-like for the self image and unset pairs)
-    for (int j = lane; j < N; j += 32) {
+    group_sync();  // the group has finished reading the previous row's bounds
+    for (int j = sub * 32 + lane; j < N; j += 32 * wpr) {
       const unsigned long long k = kr[j];
       float uj = __int_as_float(0x7f800000);  // +inf: never among the smallest
       if (j != img && k != ~0ull) uj = key_value(k) * hi_scale + bound(j);
       u[j] = uj;
     }
-    __syncwarp();
+    group_sync();
     // T = the rank_hi-th smallest U_j: the largest bit pattern t with #{U < t} < rank_hi.
     uint32_t lo = 0u, hi = 0x7f800001u;
     while (hi - lo > 1u) {
@@ -459,20 +465,23 @@ fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const
 }
 
 // Rows per CTA, threads and warps per row: 32 rows of 8 one-row warps while they fit in
-// shared memory; when fewer rows fit (large pools), 16 warps, two per row.
+// shared memory; when fewer rows fit (large pools), 24 warps in groups sharing a row
+// (registers allow 768 threads of this kernel per SM).
 int refine_rows_per_cta(int n_images, int* pitch, size_t* smem, int* threads, int* wpr) {
   int rows = 32;
   const int pt = n_images + ((2 - n_images % 2) % 2);  // even, so the 8-byte keys stay aligned
-  auto bytes_for = [&](int r, int warps) { return (size_t)r * pt * (8 + 4 + 4) + (size_t)warps * pt * 4; };
-  while (rows > 1 && (long long)bytes_for(rows, kRefineThreads / 32) > smem_optin() - 4096) rows >>= 1;
+  auto bytes_for = [&](int r, int groups) { return (size_t)r * pt * (8 + 4 + 4) + (size_t)groups * pt * 4; };
+  // groups: 8 one-row warps for 32 rows, else one group per row
+  while (rows > 1 && (long long)bytes_for(rows, rows < 32 ? rows : kRefineThreads / 32) > smem_optin() - 4096)
+    rows >>= 1;
   *threads = kRefineThreads;
   *wpr = 1;
-  if (rows < 32 && (long long)bytes_for(rows, kRefineMaxThreads / 32) <= smem_optin() - 4096) {
-    *threads = kRefineMaxThreads;
-    *wpr = 2;
+  if (rows < 32) {
+    *wpr = std::max(1, (kRefineMaxThreads / 32) / rows);
+    *threads = 32 * rows * *wpr;
   }
   *pitch = pt;
-  *smem = bytes_for(rows, *threads / 32);
+  *smem = bytes_for(rows, *threads / 32 / *wpr);
   return rows;
 }
 
