@@ -464,24 +464,30 @@ fallback_gather_kernel(BankPlanes bank, long long first_row, int channels, const
   }
 }
 
-// Rows per CTA, threads and warps per row: 32 rows of 8 one-row warps while they fit in
-// shared memory; when fewer rows fit (large pools), 24 warps in groups sharing a row
-// (registers allow 768 threads of this kernel per SM).
+// Rows per CTA, threads and warps per row.  Eight one-row warps per CTA over the most rows
+// (32, 16 or 8) that still let three CTAs share an SM, the most its registers allow; where
+// none does (large pools), one group of warps per row (24 warps per CTA) sharing the row's
+// upper bounds.
 int refine_rows_per_cta(int n_images, int* pitch, size_t* smem, int* threads, int* wpr) {
-  int rows = 32;
   const int pt = n_images + ((2 - n_images % 2) % 2);  // even, so the 8-byte keys stay aligned
-  auto bytes_for = [&](int r, int groups) { return (size_t)r * pt * (8 + 4 + 4) + (size_t)groups * pt * 4; };
-  // groups: 8 one-row warps for 32 rows, else one group per row
-  while (rows > 1 && (long long)bytes_for(rows, rows < 32 ? rows : kRefineThreads / 32) > smem_optin() - 4096)
-    rows >>= 1;
-  *threads = kRefineThreads;
-  *wpr = 1;
-  if (rows < 32) {
-    *wpr = std::max(1, (kRefineMaxThreads / 32) / rows);
-    *threads = 32 * rows * *wpr;
-  }
+  const long long per_sm = smem_optin(), budget = per_sm - 4096;
+  auto bytes_for = [&](int r, int groups) {
+    return (long long)r * pt * (8 + 4 + 4) + (long long)groups * pt * 4;
+  };
   *pitch = pt;
-  *smem = bytes_for(rows, *threads / 32 / *wpr);
+  for (int rows = 32; rows >= 8; rows >>= 1) {
+    if (per_sm / (bytes_for(rows, 8) + 1024) >= 3) {
+      *threads = kRefineThreads;
+      *wpr = 1;
+      *smem = (size_t)bytes_for(rows, 8);
+      return rows;
+    }
+  }
+  int rows = 16;
+  while (rows > 1 && bytes_for(rows, rows) > budget) rows >>= 1;
+  *wpr = std::max(1, (kRefineMaxThreads / 32) / rows);
+  *threads = 32 * rows * *wpr;
+  *smem = (size_t)bytes_for(rows, rows);
   return rows;
 }
 
