@@ -617,3 +617,26 @@ def test_centred_banks_share_one_mean(cuda_device):
     assert kept.sum() >= rows * b
     np.testing.assert_allclose(ref[kept], want[kept], rtol=2e-5, atol=1e-7)
     assert _lib_device_error_clear()
+
+
+@pytest.mark.parametrize('n', [600, 1500])
+def test_refine_large_pools_share_rows_between_warps(cuda_device, n):
+    """Pools where fewer than 32 rows of screen tables fit a refinement CTA: at 600 images
+    16 rows with one warp each in 512-thread CTAs, at 1500 images 4 rows shared by groups of
+    six warps (the upper bounds of a row filled by the group together).  The refined table
+    equals the 3-pass exact table wherever it keeps an entry, and the interval averages agree."""
+    from musc_b200 import ops
+    p, c = 16, 32
+    z = torch.randn(n, p, c, generator=torch.Generator().manual_seed(n))
+    z = z / z.norm(dim=-1, keepdim=True)
+    rows = n * p
+    bank = ops.prep_bank(z.reshape(rows, c).to(cuda_device))
+    exact = ops.nearest_pool(bank, rows, c, p)[0]
+    b = int((n - 1) * 0.3)
+    k1, m2, _ = ops.screen_pool(bank, rows, c, p)
+    ref = ops.refine(bank, rows, c, p, 0, rows, b, k1, m2)
+    kept = ref != torch.finfo(torch.float32).max
+    assert int(kept.sum()) >= rows * b
+    torch.testing.assert_close(ref[kept], exact[kept], rtol=2e-5, atol=2e-6)
+    torch.testing.assert_close(ops.trimmed_mean(ref, 0, b), ops.trimmed_mean(exact, 0, b), rtol=2e-6, atol=2e-6)
+    assert _lib_device_error_clear()
