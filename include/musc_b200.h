@@ -362,6 +362,17 @@ int musc_b200_attention_fwd(const void* q, const void* k, const void* v, void* o
                             int batch, int tokens, int heads, int head_dim, long long qkv_row_stride,
                             long long out_row_stride, float scale, musc_b200_stream stream);
 
+/* Residual add + LayerNorm of a ViT block (models/backbone/open_clip/transformer.py:236-249,
+ * the ln_1 / ln_2 normalisations with the preceding branch's residual add fused in):
+ * per row of x [rows][channels] fp32 (updated in place), x += delta (delta: the branch's
+ * [rows][channels] output in delta_dtype, f16 or bf16, widened exactly; NULL = no add),
+ * then out = (x - mean) / sqrt(var + eps) * gamma + beta in out_dtype (f16 or bf16), with
+ * the mean and biased variance in fp32 (two-pass).  channels a multiple of 128, at most
+ * 2048; all pointers 16-byte aligned. */
+int musc_b200_add_layernorm(float* x, const void* delta, int delta_dtype, const float* gamma,
+                            const float* beta, float eps, void* out, int out_dtype, long long rows,
+                            int channels, musc_b200_stream stream);
+
 /* ------------------------------------------------------------------------
  * Copy-engine exchange between the GPUs of one node (multi-GPU pool scoring;
  * no counterpart in the reference, which is single-device).

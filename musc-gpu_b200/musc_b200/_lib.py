@@ -52,6 +52,7 @@ SIGNATURES = {
     'musc_b200_msm_workspace_bytes': (_sz, [_int, _int, _int]),
     'musc_b200_msm': (_int, [_vp, _int, _int, _int, _int, _int, _vp, _vp, _sz, _vp]),
     'musc_b200_attention_fwd': (_int, [_vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _ll, _ll, _f, _vp]),
+    'musc_b200_add_layernorm': (_int, [_vp, _vp, _int, _vp, _vp, ctypes.c_float, _vp, _int, _ll, _int, _vp]),
     'musc_b200_rscin': (_int, [_vp, _int, _int, _vp, _int, ctypes.POINTER(_int), _vp, _vp]),
     'musc_b200_score_pool_bytes': (_sz, [_int, _int, _int, _int]),
     'musc_b200_score_pool': (_int, [ctypes.POINTER(_vp), _int, _int, _int, _int, _int, _int,

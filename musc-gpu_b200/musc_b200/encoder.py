@@ -11,8 +11,9 @@ discards (``:587-591``), so they are not produced here.
 
 Numerics: the linear layers (QKV in-projection, out-projection, MLP) are
 16-bit cuBLAS GEMMs with fp32 accumulation (reduced-precision fp16 reductions
-off, as ``models/modules/_MSM_gpu.py:733-735`` does for its GEMMs); LayerNorm,
-GELU inputs and the residual stream stay fp32; attention takes 16-bit q/k/v
+off, as ``models/modules/_MSM_gpu.py:733-735`` does for its GEMMs); the residual
+stream stays fp32, and each residual add runs fused with the LayerNorm after it
+(``ops.add_layernorm``: fp32 statistics, 16-bit output for the next GEMM); attention takes 16-bit q/k/v
 with fp32 softmax and accumulation.  The 16-bit type defaults to fp16 -- the
 type the reference's GPU path runs its encoder in (``torch.cuda.amp.autocast``
 at ``models/musc.py:196``) -- and bf16 is available (``compute_dtype``).
@@ -123,19 +124,25 @@ class VisionEncoder:
         patches = images.reshape(b, 3, g, p, g, p).permute(0, 2, 4, 1, 3, 5).reshape(b, g * g, 3 * p * p)
         x = F.linear(patches.to(lp), self.conv_w).float()                       # (B, g^2, width)
         x = torch.cat([self.cls.expand(b, 1, w), x], dim=1) + self.pos
-        x = F.layer_norm(x, (w,), *self.ln_pre)
+        x = F.layer_norm(x, (w,), *self.ln_pre).contiguous()
         keep = set(int(l) for l in out_layers)
         tokens = {}
+        # Each residual add is fused with the LayerNorm that follows it (ops.add_layernorm:
+        # x += branch output in fp32, then the 16-bit normalised input of the next GEMM), so
+        # the MLP output of block i is added to x at the start of block i + 1.
+        pending = None
         for idx, blk in enumerate(self.blocks, start=1):
-            h = F.layer_norm(x, (w,), *blk['ln_1']).to(lp)
+            h = ops.add_layernorm(x, pending, *blk['ln_1'], out_dtype=lp)
+            if idx - 1 in keep:
+                tokens[idx - 1] = x.clone()                              # x after block idx - 1
             qkv = self._linear(h, blk['in_w'], blk['in_b'])                      # (B, L, 3w) 16-bit
             a = ops.attention(qkv[..., :w], qkv[..., w:2 * w], qkv[..., 2 * w:], self.heads)
-            x = x + self._linear(a, blk['out_w'], blk['out_b'])          # fp32 residual
-            h = F.layer_norm(x, (w,), *blk['ln_2']).to(lp)
+            h = ops.add_layernorm(x, self._linear(a, blk['out_w'], blk['out_b']), *blk['ln_2'], out_dtype=lp)
             h = F.gelu(self._linear(h, blk['fc_w'], blk['fc_b']))       # evaluated in fp32 by torch
-            x = x + self._linear(h, blk['proj_w'], blk['proj_b'])
-            if idx in keep:
-                tokens[idx] = x
+            pending = self._linear(h, blk['proj_w'], blk['proj_b'])
+        x = x + pending                                                  # the last block's residual
+        if len(self.blocks) in keep:
+            tokens[len(self.blocks)] = x
         pooled = F.layer_norm(x[:, 0], (w,), *self.ln_post) @ self.proj
         return pooled, [tokens[l] for l in out_layers]
 

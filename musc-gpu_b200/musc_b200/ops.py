@@ -449,6 +449,34 @@ def rscin(image_scores: torch.Tensor, cls_tokens: torch.Tensor | None,
 
 
 # --------------------------------------------------------------------------- attention
+def add_layernorm(x: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, bias: torch.Tensor,
+                  eps: float = 1e-5, out_dtype: torch.dtype = torch.float16,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x += delta`` (in place, fp32; skipped when ``delta`` is None) then
+    ``layer_norm(x) * weight + bias`` in ``out_dtype`` (fp16 / bf16): the residual add and
+    LayerNorm of a ViT block in one pass.  ``x`` ``(..., C)`` contiguous fp32 CUDA."""
+    _require_cuda(x, 'add_layernorm')
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError('add_layernorm: x must be contiguous float32')
+    c = x.shape[-1]
+    rows = x.numel() // c
+    if delta is not None:
+        if delta.shape != x.shape or delta.dtype not in (torch.float16, torch.bfloat16) or not delta.is_contiguous():
+            raise ValueError('add_layernorm: delta must be a contiguous fp16/bf16 tensor of x\'s shape')
+    if out_dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError('add_layernorm: out_dtype must be float16 or bfloat16')
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    w, b = weight.contiguous(), bias.contiguous()
+    dev = x.device
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_add_layernorm(_ptr(x), _ptr(delta), _DTYPES[delta.dtype] if delta is not None else 0,
+                                                _ptr(w), _ptr(b), float(eps), _ptr(out), _DTYPES[out_dtype], rows, c,
+                                                _stream(dev))
+        _lib.check(st, 'musc_b200_add_layernorm')
+    return out
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """``softmax(q k^T * scale) v`` per head for token-major ``(B, L, heads*64)`` views.

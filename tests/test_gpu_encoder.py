@@ -85,3 +85,25 @@ def test_backend_encode_image_seam(cuda_device):
     pooled, toks = backend.encode_image(enc, img, [1, 2])
     assert pooled.shape == (2, 768) and [t.shape for t in toks] == [(2, 1370, 1024)] * 2
     assert callable(backend.encode_image.new_aggregation) and callable(backend.encode_image.aggregate_features)
+
+
+@pytest.mark.parametrize('dt', [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize('with_delta', [True, False])
+def test_add_layernorm_matches_torch(cuda_device, dt, with_delta):
+    """The fused residual add + LayerNorm of the encoder's blocks against torch's add and
+    layer_norm: the fp32 residual bit for bit, the 16-bit output within one unit in its
+    last place (fp32 statistics summed in a different order)."""
+    import torch.nn.functional as F
+    from musc_b200 import ops
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(3, 1370, 1024, generator=g).to(cuda_device)
+    delta = (0.5 * torch.randn(3, 1370, 1024, generator=g)).to(dt).to(cuda_device) if with_delta else None
+    w = (1 + 0.1 * torch.randn(1024, generator=g)).to(cuda_device)
+    b = (0.1 * torch.randn(1024, generator=g)).to(cuda_device)
+    want_x = x + delta.float() if with_delta else x.clone()
+    ref = F.layer_norm(want_x, (1024,), w, b, 1e-5)
+    got = ops.add_layernorm(x, delta, w, b, out_dtype=dt)
+    assert torch.equal(x, want_x)
+    ulp = 2.0 ** -10 if dt == torch.float16 else 2.0 ** -7
+    err = (got.float() - ref).abs()
+    assert bool((err <= ulp * ref.abs().clamp_min(2.0 ** -6) + 1e-6).all())
