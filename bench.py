@@ -59,9 +59,10 @@ def _args():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--pool', type=int, default=None, help='pool size (default: the config\'s)')
-    ap.add_argument('--config', default='2', choices=['1', '2', '3', '4', '5'],
+    ap.add_argument('--config', default='2', choices=['1', '2', '3', '4', '5', 'images'],
                     help='BASELINE.json config: 1 (N=16, the reference arm runs it in full), 2 (default, '
-                         'the metric\'s), 3 super-fast, 4 N=1024, 5 encoder end to end')
+                         'the metric\'s), 3 super-fast, 4 N=1024, 5 encoder end to end; "images" = the '
+                         'pool-image preprocessing ahead of the encoder (its own metric)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--collective-sms', type=int, default=0,
                     help='SMs left free for NCCL during each bank GEMM (multi-GPU; 0 = none)')
@@ -610,8 +611,144 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------- image preprocessing
+IMG_METRIC = 'pool images preprocessed/sec (900x900 RGB -> 3x518x518 fp32, CLIP bicubic transform)'
+IMG_H = IMG_W = 900
+IMG_OUT = 518
+
+
+def _img_pool(n: int, seed: int = 3):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 256, (n, IMG_H, IMG_W, 3), dtype=np.uint8)
+
+
+def images_cpu_measure(n_sample: int) -> dict:
+    """The reference's per-image transform (PIL bicubic resize, ToTensor, Normalize; the
+    torchvision classes of ``open_clip/transform.py:124-133``) on ``n_sample`` images, one
+    image per host thread as the reference's threaded loader runs them."""
+    from concurrent.futures import ThreadPoolExecutor
+    import torch
+    from PIL import Image
+    sys.path.insert(0, str(REPO))
+    from oracle import torch_cpu
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(1)
+    tf = torch_cpu.clip_image_transform(IMG_OUT)
+    pil = [Image.fromarray(a) for a in _img_pool(min(n_sample, 8), seed=4)]
+    with ThreadPoolExecutor(max_workers=cores) as ex:
+        list(ex.map(tf, pil[:2]))
+        t0 = time.perf_counter()
+        list(ex.map(tf, [pil[i % len(pil)] for i in range(n_sample)]))
+        wall = time.perf_counter() - t0
+    return {'value': n_sample / wall, 'cores': cores, 'wall_s': wall,
+            'sample': f'{n_sample} images of {IMG_H}x{IMG_W} through the torchvision/PIL transform, '
+                      f'{cores} threads, torch intra-op threads 1'}
+
+
+def run_images_reference(args):
+    if int(os.environ.get('RANK', '0')) != 0:
+        return
+    n_sample = 4 * (os.cpu_count() or 1)
+    ms = []
+    for i in range(args.warmup + args.steps):
+        m = images_cpu_measure(n_sample)
+        if i >= args.warmup:
+            ms.append(m)
+    value = statistics.median(x['value'] for x in ms)
+    line = {'metric': IMG_METRIC, 'value': value, 'unit': UNIT, 'n_gpus': 1, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': statistics.median(x['wall_s'] for x in ms) * 1e3,
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8 -> f32',
+            'data': 'synthetic', 'impl': 'reference',
+            'config': {'workload': f'{n_sample} images per step (sample), {IMG_H}x{IMG_W} -> {IMG_OUT}'},
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': ms[0]['cores'], 'kind': 'reference',
+                             'sample': ms[0]['sample']},
+            'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_images(args):
+    """``value``: the device transform over a resident batch of ``--pool`` (default 200, the
+    config-5 pool) 900 x 900 images (486 MB in, 644 MB out: no L2 flush needed); ``e2e``: the
+    loader's path from host arrays (pinned staging, H2D on the copy stream, the kernels), the
+    (B, 3, 518, 518) result left on the device for the encoder (no D2H)."""
+    import torch
+    from musc_b200 import ops
+    from musc_b200.loader import DeviceImageLoader
+    if int(os.environ.get('WORLD_SIZE', '1')) != 1:
+        raise SystemExit('--config images runs on one GPU')
+    n = args.pool or 200
+    dev = torch.device('cuda', 0)
+    host = _img_pool(n)
+    images = torch.from_numpy(host).to(dev)
+    out = torch.empty((n, 3, IMG_OUT, IMG_OUT), dtype=torch.float32, device=dev)
+    ws = torch.empty(ops.preprocess_workspace_bytes(IMG_H, IMG_W, IMG_OUT, IMG_OUT), dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        ops.preprocess_images(images, IMG_OUT, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for k in range(args.steps):
+            starts[k].record()
+            ops.preprocess_images(images, IMG_OUT, out=out, workspace=ws)
+            ends[k].record()
+        t1.record()
+        torch.cuda.synchronize()
+    elapsed_ms = t0.elapsed_time(t1)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    # parity of the timed output: a sampled image against the oracle restatement
+    sys.path.insert(0, str(REPO))
+    from oracle import image as oimage
+    probe = [0, n // 2, n - 1]
+    exact = all(oimage.preprocess(host[i], IMG_OUT).view('uint32').tolist()
+                == out[i].cpu().numpy().view('uint32').tolist() for i in probe)
+    # e2e through the loader from host arrays
+    loader = DeviceImageLoader([], device=dev)
+    arrays = [host[i] for i in range(n)]
+    for k in range(args.warmup):
+        loader.preprocess(arrays, slot=k % 2)
+    torch.cuda.synchronize()
+    e0 = time.perf_counter()
+    for k in range(args.steps):
+        loader.preprocess(arrays, slot=k % 2)
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - e0) / args.steps
+    peaks, peak_kind = _peaks()
+    algo_bytes = n * (IMG_H * IMG_W * 3 + 3 * IMG_OUT * IMG_OUT * 4)
+    achieved = algo_bytes / (launch_ms / 1e3) / 1e9
+    ms_per_step = elapsed_ms / args.steps
+    line = {'metric': IMG_METRIC, 'value': n / (ms_per_step / 1e3), 'unit': UNIT, 'n_gpus': 1,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms_per_step, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8 -> f32 (int32 fixed-point resample)',
+            'data': 'synthetic',
+            'config': {'workload': f'{n} images {IMG_H}x{IMG_W}x3 u8 -> 3x{IMG_OUT}x{IMG_OUT} f32 per step',
+                       'l2': 'inputs + outputs 1.13 GB > L2, no flush'},
+            'e2e': {'value': n / e2e_s, 'unit': UNIT, 'h2d_bytes_per_step': int(host.nbytes),
+                    'd2h_bytes_per_step': 0, 'note': 'host arrays -> pinned staging -> H2D -> kernels; '
+                                                     'the result stays on the device for the encoder'},
+            'roofline': {'kernel': 'resample_kernel (+ tables_kernel)', 'bound': 'hbm', 'achieved': achieved,
+                         'peak': peaks['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / peaks['hbm_gbs'],
+                         'traffic': None, 'algorithmic_bytes_per_launch': algo_bytes,
+                         'launch_ms': launch_ms, 'peak_kind': f'{peak_kind} HBM copy'},
+            'gpu_launches': 2 * args.steps, 'clocks': clocks.summary(),
+            'parity': {'images_checked': probe, 'bit_exact_vs_oracle': exact}}
+    if not args.no_cpu_baseline:
+        m = images_cpu_measure(4 * (os.cpu_count() or 1))
+        line['cpu_baseline'] = {'value': m['value'], 'unit': UNIT, 'cores': m['cores'], 'kind': 'reference',
+                                'sample': m['sample'], 'timed_s': round(m['wall_s'], 2)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = _args()
+    if args.config == 'images':
+        (run_images_reference if args.impl == 'reference' else run_images)(args)
+        return
     if args.impl == 'reference':
         run_reference(args)
     else:

@@ -374,6 +374,34 @@ int musc_b200_add_layernorm(float* x, const void* delta, int delta_dtype, const 
                             int channels, musc_b200_stream stream);
 
 /* ------------------------------------------------------------------------
+ * Pool-image preprocessing: the evaluation transform the reference applies to
+ * each image before the encoder -- Resize((out_h, out_w), BICUBIC), CenterCrop
+ * of the same size (the identity), ToTensor, Normalize(mean, std)
+ * (models/backbone/open_clip/transform.py:124-133, applied per item in
+ * datasets/mvtec.py:98-99, batched by models/modules/_loader.py:8-43 and
+ * moved to the device at models/musc.py:197) -- on the device, bit for bit.
+ * The resize is Pillow's antialiased separable resample (fixed-point weights
+ * with 22 fractional bits, 8-bit horizontal pass, then vertical pass);
+ * MUSC_B200_BILINEAR gives Pillow's bilinear, the reference's non-CLIP path
+ * (datasets/mvtec.py:53-60).
+ * images: n_images 8-bit RGB images, H x W x 3 row-major (decoded on the host,
+ * e.g. PIL convert("RGB")), image i at images + i * image_stride_bytes.
+ * mean, std: 3 host floats each (copied at the call).  out: n_images x 3 x
+ * out_h x out_w in out_dtype (F32 = the reference's tensor bit for bit; F16 /
+ * BF16 = that tensor rounded to nearest).  An input side may be at most 15.75x
+ * (bicubic) / 31.5x (bilinear) its output side.  workspace: the two axes'
+ * weight tables, musc_b200_preprocess_workspace_bytes (0 = invalid sizes).
+ * ---------------------------------------------------------------------- */
+enum musc_b200_filter { MUSC_B200_BICUBIC = 0, MUSC_B200_BILINEAR = 1 };
+
+size_t musc_b200_preprocess_workspace_bytes(int in_h, int in_w, int out_h, int out_w, int filter);
+
+int musc_b200_preprocess_images(const uint8_t* images, int n_images, int in_h, int in_w,
+                                long long image_stride_bytes, int out_h, int out_w, int filter,
+                                const float* mean, const float* std, int out_dtype, void* out,
+                                void* workspace, size_t workspace_bytes, musc_b200_stream stream);
+
+/* ------------------------------------------------------------------------
  * Copy-engine exchange between the GPUs of one node (multi-GPU pool scoring;
  * no counterpart in the reference, which is single-device).
  *

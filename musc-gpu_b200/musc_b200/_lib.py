@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().with_name('libmusc_b200.so')
 
 OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_WORKSPACE, ERR_TIMEOUT = range(6)
 F32, F16, BF16 = 0, 1, 2
+BICUBIC, BILINEAR = 0, 1
 
 _vp, _ll, _int, _sz, _f = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
 
@@ -53,6 +54,9 @@ SIGNATURES = {
     'musc_b200_msm': (_int, [_vp, _int, _int, _int, _int, _int, _vp, _vp, _sz, _vp]),
     'musc_b200_attention_fwd': (_int, [_vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _ll, _ll, _f, _vp]),
     'musc_b200_add_layernorm': (_int, [_vp, _vp, _int, _vp, _vp, ctypes.c_float, _vp, _int, _ll, _int, _vp]),
+    'musc_b200_preprocess_workspace_bytes': (_sz, [_int, _int, _int, _int, _int]),
+    'musc_b200_preprocess_images': (_int, [_vp, _int, _int, _int, _ll, _int, _int, _int,
+                                           ctypes.POINTER(_f), ctypes.POINTER(_f), _int, _vp, _vp, _sz, _vp]),
     'musc_b200_rscin': (_int, [_vp, _int, _int, _vp, _int, ctypes.POINTER(_int), _vp, _vp]),
     'musc_b200_score_pool_bytes': (_sz, [_int, _int, _int, _int]),
     'musc_b200_score_pool': (_int, [ctypes.POINTER(_vp), _int, _int, _int, _int, _int, _int,

@@ -507,3 +507,57 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, sca
                                                 _stream(dev))
         _lib.check(st, 'musc_b200_attention_fwd')
     return out
+
+
+OPENAI_MEAN = (0.48145466, 0.4578275, 0.40821073)
+OPENAI_STD = (0.26862954, 0.26130258, 0.27577711)
+_FILTERS = {'bicubic': _lib.BICUBIC, 'bilinear': _lib.BILINEAR}
+
+
+def preprocess_workspace_bytes(in_h: int, in_w: int, out_h: int, out_w: int, filter: str = 'bicubic') -> int:
+    if filter not in _FILTERS:
+        raise ValueError("preprocess_images: filter must be 'bicubic' or 'bilinear'")
+    n = _lib.lib().musc_b200_preprocess_workspace_bytes(in_h, in_w, out_h, out_w, _FILTERS[filter])
+    if n == 0:
+        raise ValueError(f'preprocess_images: unsupported sizes {in_h}x{in_w} -> {out_h}x{out_w}')
+    return n
+
+
+def preprocess_images(images: torch.Tensor, size: int | tuple[int, int] = 518, filter: str = 'bicubic',
+                      mean: Sequence[float] = OPENAI_MEAN, std: Sequence[float] = OPENAI_STD,
+                      out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's evaluation transform on the device: ``(B, H, W, 3)`` uint8 RGB ->
+    ``(B, 3, size, size)`` -- Pillow's antialiased resize (bicubic, or bilinear), ToTensor,
+    Normalize -- bit for bit with ``open_clip/transform.py:124-133`` for fp32 output.
+
+    ``images`` may be a batch view whose images are evenly spaced in memory with contiguous
+    rows (e.g. a slice of a larger staging buffer)."""
+    _require_cuda(images, 'preprocess_images')
+    if images.dtype != torch.uint8 or images.ndim != 4 or images.shape[-1] != 3:
+        raise ValueError('preprocess_images: images must be a (B, H, W, 3) uint8 tensor')
+    b, h, w, _ = images.shape
+    if images.stride()[1:] != (3 * w, 3, 1):
+        raise ValueError('preprocess_images: each image must be H x W x 3 with contiguous rows')
+    out_h, out_w = (size, size) if isinstance(size, int) else (int(size[0]), int(size[1]))
+    if out_dtype not in _DTYPES:
+        raise ValueError('preprocess_images: out_dtype must be float32, float16 or bfloat16')
+    if len(mean) != 3 or len(std) != 3:
+        raise ValueError('preprocess_images: mean and std need 3 values')
+    dev = images.device
+    if out is None:
+        out = torch.empty((b, 3, out_h, out_w), dtype=out_dtype, device=dev)
+    elif out.shape != (b, 3, out_h, out_w) or out.dtype != out_dtype or not out.is_contiguous():
+        raise ValueError('preprocess_images: out must be a contiguous (B, 3, out_h, out_w) tensor of out_dtype')
+    ws_bytes = preprocess_workspace_bytes(h, w, out_h, out_w, filter)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    m = (ctypes.c_float * 3)(*[float(v) for v in mean])
+    s = (ctypes.c_float * 3)(*[float(v) for v in std])
+    stride = images.stride(0) if b > 1 else 3 * h * w
+    with torch.cuda.device(dev):
+        st = _lib.lib().musc_b200_preprocess_images(_ptr(images), b, h, w, stride, out_h, out_w, _FILTERS[filter],
+                                                    m, s, _DTYPES[out_dtype], _ptr(out), _ptr(workspace),
+                                                    workspace.numel(), _stream(dev))
+        _lib.check(st, 'musc_b200_preprocess_images')
+    return out

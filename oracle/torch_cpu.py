@@ -13,6 +13,7 @@ understate it).  Its results are pinned against the same golden fixtures.
   (``PatchMaker.patchify``, ``:16-34``; r = 1 is the plain reshape of ``:93-94``), the
   per-channel window mean by ``adaptive_avg_pool1d`` over the flattened ``(C, r, r)``
   patch (``MeanMapper``, ``:58-61``), then the L2 normalisation of ``models/musc.py:238``.
+* ``clip_image_transform`` -- the per-image evaluation transform of the pool images.
 * ``msm_rows`` -- ``compute_scores_fast`` (``models/modules/_MSM.py:10-30``) for one
   query image: ``cdist`` against every other image's patches, the per-image minimum, the
   two ``topk`` passes of the interval ``[k_min, k_max)`` and the mean.
@@ -87,3 +88,20 @@ def msm(z: torch.Tensor, topmin_min: float = 0.0, topmin_max: float = 0.3) -> to
     """``(N, P, C)`` -> ``(N, P)`` float64 (``_MSM.py:53-59``)."""
     k_min, k_max = interval(z.shape[0], topmin_min, topmin_max)
     return torch.stack([msm_rows(z, i, k_min, k_max) for i in range(z.shape[0])]).double()
+
+
+def clip_image_transform(size: int = 518):
+    """The reference's CLIP evaluation transform (``models/backbone/open_clip/transform.py:124-133``)
+    built from the same torchvision classes: ``Resize((size, size), BICUBIC)``,
+    ``CenterCrop((size, size))``, RGB conversion, ``ToTensor()``, ``Normalize`` with the OpenAI
+    constants (``constants.py:1-2``).  Applied to a PIL image it gives the ``(3, size, size)``
+    fp32 tensor the reference's dataset returns (``datasets/mvtec.py:98-99``)."""
+    from torchvision import transforms
+    from torchvision.transforms import InterpolationMode
+    return transforms.Compose([
+        transforms.Resize((size, size), interpolation=InterpolationMode.BICUBIC),
+        transforms.CenterCrop((size, size)),
+        lambda image: image.convert('RGB'),
+        transforms.ToTensor(),
+        transforms.Normalize(mean=(0.48145466, 0.4578275, 0.40821073), std=(0.26862954, 0.26130258, 0.27577711)),
+    ])

@@ -11,7 +11,8 @@ The script imports the reference's ``original`` modules --
 (``aggregate_features``), ``models/modules/_super_fast.py``
 (``SuperFastAggregation``), ``models/modules/_RsCIN.py`` (``RsCIN``) and
 the CLIP ``VisionTransformer``
-(``models/backbone/open_clip/transformer.py``) -- and evaluates the score
+(``models/backbone/open_clip/transformer.py``) and its evaluation image transform
+(``models/backbone/open_clip/transform.py``) -- and evaluates the score
 reduction of ``models/musc.py:259-288`` with the same torch calls.  Inputs are
 either stored in the fixture (small cases) or regenerated with the recorded
 seed (the N=16 prototype-mixture pool from ``musc_b200.synthetic``; the
@@ -210,6 +211,51 @@ def make_encoder_pool(MSM, LNAMD, reference: str) -> dict:
             'scores': scores.numpy(), 'maps': maps, 'image_max': image_max}
 
 
+def _reference_image_transform(reference: str):
+    """``image_transform`` of the reference's open_clip (``models/backbone/open_clip/transform.py``),
+    under the same stub package as the ViT."""
+    import importlib
+    _reference_vit_class(reference)
+    return importlib.import_module('reference_open_clip.transform').image_transform
+
+
+IMAGE_HASHED = {'mvtec900': (900, 900, 518, 11), 'visa1000x1500': (1000, 1500, 518, 12),
+                'small_up': (200, 240, 518, 13)}
+
+
+def make_image_preprocess(reference: str) -> dict:
+    """The reference's evaluation transform (``transform.py:124-133``: Resize BICUBIC, CenterCrop,
+    ToTensor, Normalize with the OpenAI constants) on seeded 8-bit RGB images: small cases with
+    inputs and outputs stored, full-size cases (MVTec's 900 x 900, a VisA-like 1000 x 1500, an
+    up-sampled 200 x 240) regenerated from their seeds and pinned by the SHA-256 of the fp32
+    output bytes.  ``bilinear`` is the non-CLIP dataset transform (``datasets/mvtec.py:53-60``,
+    ``Resize((resize, resize))`` + ``CenterCrop(imagesize)`` with resize == imagesize, ImageNet
+    constants), built from the same torchvision classes."""
+    import hashlib
+    from PIL import Image
+    from torchvision import transforms
+    image_transform = _reference_image_transform(reference)
+    rng = np.random.default_rng(4242)
+    out = {}
+    for name, (h, w, size) in {'up': (37, 53, 64), 'down': (300, 260, 112), 'wide': (64, 200, 64),
+                               'tall': (181, 47, 40), 'same': (64, 64, 64)}.items():
+        arr = rng.integers(0, 256, (h, w, 3), dtype=np.uint8)
+        out[f'{name}_in'] = arr
+        out[f'{name}_out'] = image_transform(size, is_train=False)(Image.fromarray(arr)).numpy()
+    arr = rng.integers(0, 256, (90, 77, 3), dtype=np.uint8)
+    mean, std = [0.485, 0.456, 0.406], [0.229, 0.224, 0.225]
+    bilinear = transforms.Compose([transforms.Resize((64, 64)), transforms.CenterCrop(64), transforms.ToTensor(),
+                                   transforms.Normalize(mean=mean, std=std)])
+    out['bilinear_in'] = arr
+    out['bilinear_out'] = bilinear(Image.fromarray(arr)).numpy()
+    for name, (h, w, size, seed) in IMAGE_HASHED.items():
+        arr = np.random.default_rng(seed).integers(0, 256, (h, w, 3), dtype=np.uint8)
+        res = image_transform(size, is_train=False)(Image.fromarray(arr)).numpy()
+        out[f'{name}_sha256'] = np.array(hashlib.sha256(np.ascontiguousarray(res).tobytes()).hexdigest())
+        out[f'{name}_probe'] = res[:, ::37, ::41].copy()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True)
@@ -222,7 +268,8 @@ def main() -> None:
             'reduce_small': make_reduce_small,
             'pool16': lambda: make_pool16(MSM, LNAMD, encoder_gpu),
             'encoder_pool6': lambda: make_encoder_pool(MSM, LNAMD, args.reference),
-            'rscin_small': lambda: make_rscin_small(args.reference)}
+            'rscin_small': lambda: make_rscin_small(args.reference),
+            'image_preprocess': lambda: make_image_preprocess(args.reference)}
     for name, job in jobs.items():
         if args.only and name not in args.only.split(','):
             continue

@@ -9,7 +9,7 @@ two files from the reference checkout into a temporary directory, applies the bl
 * the patched ``select_backend`` keeps the reference's behaviour for its own names and
   raises for ``b200`` / ``b200_super_fast`` where there is no B200 (no fallback), and the
   patched ``configure_backend`` does the same for the super-fast preset;
-* the patched ``musc.py`` still compiles and selects the ``b200`` operators.
+* the patched ``musc.py`` still compiles and selects the ``b200`` operators and image loader.
 
 The reference checkout is found through ``MUSC_REFERENCE`` (default: the directory
 ``reference`` beside this repository); where it is absent the test is skipped.
@@ -88,5 +88,8 @@ def test_patched_musc_selects_the_b200_operators(patched):
     assert "'b200', 'b200_super_fast'" in src
     assert 'gpu_msm = b200.MSM' in src and 'b200.encode_image' in src
     assert 'b200_rscin(ac_score, class_tokens, k_list=k_score, device=self.device)' in src
+    # pool images: decoded by the dataset, preprocessed on the device by the b200 loader
+    assert 'test_dataset.transform_img = RawRGB()' in src and 'DeviceImageLoader(' in src
+    assert 'from models.modules._loader import ThreadedDatasetLoader' in src
     # the reference's own GPU imports are still there for its own backends
     assert 'from models.modules._MSM_gpu import MSM as gpu_msm' in src

@@ -117,3 +117,49 @@ def test_timed_cpu_port_matches_reference_exactly():
         lo, hi = (float(v) for v in g[f'{c}_ranks'])
         got = torch_cpu.msm(torch.from_numpy(g[f'{c}_z']), lo, hi).numpy()
         np.testing.assert_array_equal(got, g[f'{c}_scores'])
+
+
+IMAGE_CASES = ('up', 'down', 'wide', 'tall', 'same')
+IMAGE_SIZES = {'up': 64, 'down': 112, 'wide': 64, 'tall': 40, 'same': 64}
+
+
+@pytest.mark.parametrize('case', IMAGE_CASES + ('bilinear',))
+def test_image_oracle_matches_reference_transform(case):
+    """The numpy restatement of Pillow's resample + ToTensor + Normalize equals the
+    reference's own transform bit for bit (``open_clip/transform.py:124-133``; the bilinear
+    case is ``datasets/mvtec.py:53-60``)."""
+    from oracle import image as oimage
+    g = golden('image_preprocess')
+    img = g[f'{case}_in']
+    if case == 'bilinear':
+        got = oimage.preprocess(img, 64, oimage.BILINEAR, (0.485, 0.456, 0.406), (0.229, 0.224, 0.225))
+    else:
+        got = oimage.preprocess(img, IMAGE_SIZES[case])
+    want = g[f'{case}_out']
+    assert got.dtype == np.float32 and got.shape == want.shape
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_image_oracle_full_size_hashes():
+    """MVTec-sized (900 x 900), VisA-like (1000 x 1500) and up-sampled (200 x 240) images,
+    regenerated from their seeds: the oracle's fp32 bytes hash to the reference's."""
+    import hashlib
+    from oracle import image as oimage
+    g = golden('image_preprocess')
+    for name, (h, w, size, seed) in {'mvtec900': (900, 900, 518, 11), 'visa1000x1500': (1000, 1500, 518, 12),
+                                     'small_up': (200, 240, 518, 13)}.items():
+        img = np.random.default_rng(seed).integers(0, 256, (h, w, 3), dtype=np.uint8)
+        got = oimage.preprocess(img, size)
+        assert np.array_equal(got[:, ::37, ::41], g[f'{name}_probe']), name
+        assert hashlib.sha256(got.tobytes()).hexdigest() == str(g[f'{name}_sha256']), name
+
+
+def test_timed_image_transform_matches_reference():
+    """The CPU baseline's image transform (``oracle.torch_cpu.clip_image_transform``) gives the
+    reference transform's tensors bit for bit."""
+    from PIL import Image
+    from oracle import torch_cpu
+    g = golden('image_preprocess')
+    for case in IMAGE_CASES:
+        got = torch_cpu.clip_image_transform(IMAGE_SIZES[case])(Image.fromarray(g[f'{case}_in'])).numpy()
+        assert np.array_equal(got.view(np.uint32), g[f'{case}_out'].view(np.uint32)), case
