@@ -141,7 +141,9 @@ __global__ void __launch_bounds__(kThreads) resample_kernel(Params p) {
   for (int i = threadIdx.x; i < 3 * 256; i += kThreads) {
     int c = i >> 8;
     float x = __fdiv_rn(static_cast<float>(i & 255), 255.0f);
-    lut[i] = __fdiv_rn(__fsub_rn(x, p.mean[c]), p.stdev[c]);
+    float m = c == 0 ? p.mean[0] : (c == 1 ? p.mean[1] : p.mean[2]);
+    float sd = c == 0 ? p.stdev[0] : (c == 1 ? p.stdev[1] : p.stdev[2]);
+    lut[i] = __fdiv_rn(__fsub_rn(x, m), sd);
   }
 
   // Input rows of the band: [r0, r0 + rows).
@@ -213,11 +215,153 @@ __global__ void __launch_bounds__(kThreads) resample_kernel(Params p) {
   }
 }
 
+// Staged form for the common case (both axes resized, at most 17 horizontal
+// taps: an input at most 4x its output).  The band's input rows are copied
+// into shared memory with 16-byte loads; the horizontal pass gives each thread
+// one output column with its weights in registers and a run of rows; the
+// vertical pass gives each thread four adjacent columns of one channel (one
+// 32-bit shared load per tap) with the row's weights broadcast from shared
+// memory.  Shared memory: LUT | band rows' vertical bounds + weights | 8-bit
+// horizontal result [3][max_rows][pitch] | input rows (+ slack for the taps
+// past a row's end, whose weights are zero).
+constexpr int kRowsPerItem = 2;
+
+// Threads of the staged kernel: 512 for up to 9 taps (64 registers, two CTAs per SM),
+// 256 for the wider tap buckets.
+__host__ __device__ constexpr int staged_threads(int kh) { return kh <= 9 ? 512 : 256; }
+
+__host__ __device__ inline int band_pitch(int out_w) { return (out_w + 3) & ~3; }
+
+__host__ __device__ inline size_t staged_smem(int ty, int kv, int max_rows, int out_w, long long row_bytes,
+                                              int kh_max) {
+  size_t off = 3 * 256 * sizeof(float) + 16 * sizeof(int2);
+  off += (static_cast<size_t>(ty) * kv * sizeof(int) + 15) & ~static_cast<size_t>(15);
+  off += 3ULL * max_rows * band_pitch(out_w);
+  off = (off + 15) & ~static_cast<size_t>(15);
+  return off + static_cast<size_t>(max_rows) * row_bytes + 16 + 3 * kh_max + 16;
+}
+
+template <typename OutT, int KH>
+__global__ void __launch_bounds__(staged_threads(KH), 2) resample_staged_kernel(Params p) {
+  constexpr int kT = staged_threads(KH);
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* lut = reinterpret_cast<float*>(smem);
+  int2* vb_s = reinterpret_cast<int2*>(smem + 3 * 256 * sizeof(float));
+  int* vw_s = reinterpret_cast<int*>(vb_s + 16);
+  uint8_t* band = reinterpret_cast<uint8_t*>(vw_s) + ((p.ty * p.kv * sizeof(int) + 15) & ~static_cast<size_t>(15));
+  const int pitch = band_pitch(p.out_w);
+  const int plane = p.max_rows * pitch;
+  uint8_t* in_s = band + ((3 * plane + 15) & ~15);
+  const int img = blockIdx.y;
+  const int y0 = blockIdx.x * p.ty;
+  const int y1 = min(y0 + p.ty, p.out_h);
+  const int tid = threadIdx.x;
+  const long long row_bytes = 3LL * p.in_w;
+
+  for (int i = tid; i < 3 * 256; i += kT) {
+    int c = i >> 8;
+    float x = __fdiv_rn(static_cast<float>(i & 255), 255.0f);
+    float m = c == 0 ? p.mean[0] : (c == 1 ? p.mean[1] : p.mean[2]);
+    float sd = c == 0 ? p.stdev[0] : (c == 1 ? p.stdev[1] : p.stdev[2]);
+    lut[i] = __fdiv_rn(__fsub_rn(x, m), sd);
+  }
+  for (int i = tid; i < (y1 - y0) * p.kv; i += kT) {
+    int dy = i / p.kv;
+    vw_s[i] = __ldg(p.vw + static_cast<long long>(y0) * p.kv + i);
+    if (i - dy * p.kv == 0) vb_s[dy] = p.vb[y0 + dy];
+  }
+  int2 first = p.vb[y0], last = p.vb[y1 - 1];
+  const int r0 = first.x;
+  const int rows = min(last.x + last.y - first.x, p.max_rows);   // the min never binds (band_rows)
+
+  // Input rows [r0, r0 + rows) -> in_s[off0 ...]: whole 16-byte chunks by vector loads,
+  // the partial chunks at both ends byte by byte (every access inside the image).
+  {
+    const uint8_t* start = p.images + static_cast<long long>(img) * p.image_stride + r0 * row_bytes;
+    const long long n = rows * row_bytes;
+    const int off0 = static_cast<int>(reinterpret_cast<uintptr_t>(start) & 15);
+    const uint8_t* a0 = start - off0;
+    const long long chunks = (off0 + n + 15) >> 4;
+    for (long long k = tid; k < chunks; k += kT) {
+      long long lo = k << 4, hi = lo + 16;
+      if (lo >= off0 && hi <= off0 + n) {
+        *reinterpret_cast<uint4*>(in_s + lo) = __ldg(reinterpret_cast<const uint4*>(a0 + lo));
+      } else {
+        for (long long b = max(lo, static_cast<long long>(off0)); b < min(hi, off0 + n); ++b) in_s[b] = __ldg(a0 + b);
+      }
+    }
+    in_s += off0;
+  }
+  __syncthreads();
+
+  // Horizontal pass: item = (column, run of kRowsPerItem rows).
+  const int runs = (rows + kRowsPerItem - 1) / kRowsPerItem;
+  for (int i = tid; i < runs * p.out_w; i += kT) {
+    int run = i / p.out_w;
+    int x = i - run * p.out_w;
+    int2 b = __ldg(p.hb + x);
+    const int* k = p.hw + static_cast<long long>(x) * p.kh;
+    int w[KH];
+#pragma unroll
+    for (int t = 0; t < KH; ++t) w[t] = t < p.kh ? __ldg(k + t) : 0;   // zero past the taps
+    const uint8_t* base = in_s + 3 * b.x;
+    int rend = min(run * kRowsPerItem + kRowsPerItem, rows);
+    for (int r = run * kRowsPerItem; r < rend; ++r) {
+      const uint8_t* px = base + r * row_bytes;
+      int a0 = 1 << (kPrecisionBits - 1), a1 = a0, a2 = a0;
+#pragma unroll
+      for (int t = 0; t < KH; ++t) {
+        a0 += static_cast<int>(px[3 * t + 0]) * w[t];
+        a1 += static_cast<int>(px[3 * t + 1]) * w[t];
+        a2 += static_cast<int>(px[3 * t + 2]) * w[t];
+      }
+      uint8_t* dst = band + r * pitch + x;
+      dst[0] = static_cast<uint8_t>(clip8(a0));
+      dst[plane] = static_cast<uint8_t>(clip8(a1));
+      dst[2 * plane] = static_cast<uint8_t>(clip8(a2));
+    }
+  }
+  __syncthreads();
+
+  // Vertical pass: item = (output row, channel, four columns).
+  OutT* out = reinterpret_cast<OutT*>(p.out) + static_cast<long long>(img) * 3 * p.out_h * p.out_w;
+  const int nq = pitch >> 2;
+  for (int i = tid; i < (y1 - y0) * 3 * nq; i += kT) {
+    const int dy = i / (3 * nq);
+    const int y = y0 + dy;
+    const int2 b = vb_s[dy];
+    const int f = b.x - r0;
+    const int taps = min(b.y, rows - f);   // never binds (see max_rows)
+    const int* wy = vw_s + dy * p.kv;
+    int rem = i - dy * 3 * nq;
+    int c = rem >= 2 * nq ? 2 : (rem >= nq ? 1 : 0);
+    int xq = rem - c * nq;
+    const uint32_t* col = reinterpret_cast<const uint32_t*>(band + c * plane) + xq;
+    int acc0 = 1 << (kPrecisionBits - 1), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+    for (int t = 0; t < taps; ++t) {
+      uint32_t v = col[(f + t) * nq];
+      int w = wy[t];
+      acc0 += static_cast<int>(v & 255u) * w;
+      acc1 += static_cast<int>((v >> 8) & 255u) * w;
+      acc2 += static_cast<int>((v >> 16) & 255u) * w;
+      acc3 += static_cast<int>(v >> 24) * w;
+    }
+    const float* l = lut + c * 256;
+    OutT* o = out + (static_cast<long long>(c) * p.out_h + y) * p.out_w + 4 * xq;
+    int x = 4 * xq;
+    if (x + 0 < p.out_w) o[0] = from_f32<OutT>(l[clip8(acc0)]);
+    if (x + 1 < p.out_w) o[1] = from_f32<OutT>(l[clip8(acc1)]);
+    if (x + 2 < p.out_w) o[2] = from_f32<OutT>(l[clip8(acc2)]);
+    if (x + 3 < p.out_w) o[3] = from_f32<OutT>(l[clip8(acc3)]);
+  }
+}
+
 struct Plan {
   Axis h, v;
   int need_h, need_v, ty, max_rows;
   size_t smem;
   size_t offsets[5];   // hb, hw, vb, vw, end
+  int staged_kh;       // 0 = the general kernel, else the staged kernel's tap bucket
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -236,10 +380,28 @@ int make_plan(int in_h, int in_w, int out_h, int out_w, int filter, int n_images
                 "preprocess_images: an input side is more than 15.75x (bicubic) / 31.5x (bilinear) its output side");
   plan->need_h = in_w != out_w;
   plan->need_v = in_h != out_h;
-  // Tallest band that fits the shared memory and still gives two CTAs per SM.
   int sms = n_images > 0 ? sm_count() : 148;
-  plan->ty = 0;
-  for (int ty = 16; ty >= 1; ty >>= 1) {
+  // Staged kernel: both axes resized and at most 17 horizontal taps.  Tallest band of
+  // 16, 8 or 4 rows whose shared memory lets two CTAs share an SM (and that gives two
+  // CTAs per SM over the grid, where the batch allows).
+  plan->staged_kh = 0;
+  if (plan->need_h && plan->need_v && plan->h.ksize <= 17) {
+    int kh = plan->h.ksize <= 9 ? 9 : (plan->h.ksize <= 13 ? 13 : 17);
+    for (int ty = 16; ty >= 4; ty >>= 1) {
+      int rows = band_rows(plan->v, ty, true);
+      size_t smem = staged_smem(ty, plan->v.ksize, rows, out_w, 3LL * in_w, kh);
+      if (smem > 113 * 1024) continue;
+      long long ctas = static_cast<long long>((out_h + ty - 1) / ty) * (n_images > 0 ? n_images : 1);
+      plan->staged_kh = kh;
+      plan->ty = ty;
+      plan->max_rows = rows;
+      plan->smem = smem;
+      if (ctas >= 2LL * sms) break;
+    }
+  }
+  // General kernel: tallest band that fits the shared memory and still gives two CTAs per SM.
+  if (!plan->staged_kh) plan->ty = 0;
+  for (int ty = 16; !plan->staged_kh && ty >= 1; ty >>= 1) {
     int rows = band_rows(plan->v, ty, plan->need_v);
     size_t smem = 3 * 256 * sizeof(float) + 3ULL * rows * out_w;
     if (smem > kMaxSmem) continue;
@@ -262,10 +424,14 @@ int make_plan(int in_h, int in_w, int out_h, int out_w, int filter, int n_images
 
 template <typename OutT>
 int launch(const Params& p, const Plan& plan, int n_images, cudaStream_t stream) {
-  auto kern = resample_kernel<OutT>;
+  auto kern = plan.staged_kh == 9    ? resample_staged_kernel<OutT, 9>
+              : plan.staged_kh == 13 ? resample_staged_kernel<OutT, 13>
+              : plan.staged_kh == 17 ? resample_staged_kernel<OutT, 17>
+                                     : resample_kernel<OutT>;
+  int threads = plan.staged_kh ? staged_threads(plan.staged_kh) : kThreads;
   MUSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem)));
   dim3 grid((p.out_h + p.ty - 1) / p.ty, n_images);
-  kern<<<grid, kThreads, plan.smem, stream>>>(p);
+  kern<<<grid, threads, plan.smem, stream>>>(p);
   return check_launch("resample_kernel");
 }
 

@@ -19,6 +19,7 @@ dict -- with ``"image"`` a ``(B, 3, S, S)`` device tensor on the current stream.
 """
 from __future__ import annotations
 
+import os
 from concurrent.futures import ThreadPoolExecutor
 from typing import Iterator, Sequence
 
@@ -103,6 +104,7 @@ class DeviceImageLoader:
         self._staging: list[torch.Tensor | None] = [None, None]
         self._copied: list[torch.cuda.Event | None] = [None, None]
         self._copy_stream: torch.cuda.Stream | None = None
+        self._copier: ThreadPoolExecutor | None = None
 
     def __len__(self) -> int:
         return (len(self.dataset) + self.batch_size - 1) // self.batch_size
@@ -117,44 +119,56 @@ class DeviceImageLoader:
             self._staging[slot] = buf
         return buf
 
+    _CHUNK = 16   # images per host copy / H2D / kernel step of the pipeline below
+
+    def _runs(self, arrays):
+        """(start, end, h, w): runs of equal-sized images, at most ``_CHUNK`` long."""
+        start = 0
+        while start < len(arrays):
+            h, w, _ = arrays[start].shape
+            end = start + 1
+            while end < len(arrays) and end - start < self._CHUNK and arrays[end].shape == (h, w, 3):
+                end += 1
+            yield start, end, h, w
+            start = end
+
     def preprocess(self, images: list, slot: int = 0) -> torch.Tensor:
         """``images`` (decoded ``(H, W, 3)`` uint8 arrays) -> ``(B, 3, S, S)`` on the device,
-        ordered on the current stream.  Runs of equal-sized images share one launch."""
+        ordered on the current stream.
+
+        Pipelined in runs of up to 16 equal-sized images: the host threads copy a run into
+        the pinned staging buffer while the copy stream moves the previous run to the device
+        and the current stream resamples the one before."""
         arrays = [_as_hwc_u8(im) for im in images]
         dev = self.device
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(device=dev)
+            self._copier = ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1))
         nbytes = sum(a.nbytes for a in arrays)
         host = self._stage(slot, nbytes)
-        offset = 0
-        for a in arrays:
-            host[offset:offset + a.nbytes].numpy()[:] = a.reshape(-1)
-            offset += a.nbytes
         compute = torch.cuda.current_stream(dev)
         with torch.cuda.device(dev):
+            out = torch.empty((len(arrays), 3, self.size, self.size), dtype=self.out_dtype, device=dev)
             with torch.cuda.stream(self._copy_stream):
-                # allocated on the copy stream, so the copy waits for nothing on the compute
+                # allocated on the copy stream, so the copies wait for nothing on the compute
                 # stream; record_stream keeps it alive until the compute stream is done with it
                 staged = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-                staged.copy_(host[:nbytes], non_blocking=True)
-                done = torch.cuda.Event()
-                done.record(self._copy_stream)
-            self._copied[slot] = done
-            compute.wait_event(done)
             staged.record_stream(compute)
-            out = torch.empty((len(arrays), 3, self.size, self.size), dtype=self.out_dtype, device=dev)
-            start = 0
             offset = 0
-            while start < len(arrays):
-                h, w, _ = arrays[start].shape
-                end = start
-                while end < len(arrays) and arrays[end].shape == (h, w, 3):
-                    end += 1
-                run = staged[offset:offset + (end - start) * h * w * 3].view(end - start, h, w, 3)
+            for start, end, h, w in self._runs(arrays):
+                size = (end - start) * h * w * 3
+                dst = host[offset:offset + size].numpy().reshape(end - start, h, w, 3)
+                list(self._copier.map(lambda j: np.copyto(dst[j], arrays[start + j]), range(end - start)))
+                with torch.cuda.stream(self._copy_stream):
+                    staged[offset:offset + size].copy_(host[offset:offset + size], non_blocking=True)
+                    done = torch.cuda.Event()
+                    done.record(self._copy_stream)
+                self._copied[slot] = done   # copies are ordered: the last event covers them all
+                compute.wait_event(done)
+                run = staged[offset:offset + size].view(end - start, h, w, 3)
                 ops.preprocess_images(run, self.size, self.filter, self.mean, self.std, self.out_dtype,
                                       out=out[start:end])
-                offset += (end - start) * h * w * 3
-                start = end
+                offset += size
         return out
 
     def __iter__(self):
