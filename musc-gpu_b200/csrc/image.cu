@@ -307,13 +307,26 @@ __global__ void __launch_bounds__(staged_threads(KH), 2) resample_staged_kernel(
     const uint8_t* base = in_s + 3 * b.x;
     int rend = min(run * kRowsPerItem + kRowsPerItem, rows);
     for (int r = run * kRowsPerItem; r < rend; ++r) {
+      // The 3 * KH tap bytes as 32-bit shared loads: NW aligned words from the window's
+      // aligned-down start, re-aligned to the window by funnel shifts (the last bytes may
+      // lie past the row: their weights are zero, and the slack after the staged rows
+      // covers them).
+      constexpr int NV = (3 * KH + 3) / 4, NW = NV + 1;
       const uint8_t* px = base + r * row_bytes;
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(px) & ~uintptr_t(3));
+      const int sh = static_cast<int>(reinterpret_cast<uintptr_t>(px) & 3) * 8;
+      uint32_t wv[NW];
+#pragma unroll
+      for (int k = 0; k < NW; ++k) wv[k] = wp[k];
+      uint32_t v[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k) v[k] = __funnelshift_r(wv[k], wv[k + 1], sh);
       int a0 = 1 << (kPrecisionBits - 1), a1 = a0, a2 = a0;
 #pragma unroll
       for (int t = 0; t < KH; ++t) {
-        a0 += static_cast<int>(px[3 * t + 0]) * w[t];
-        a1 += static_cast<int>(px[3 * t + 1]) * w[t];
-        a2 += static_cast<int>(px[3 * t + 2]) * w[t];
+        a0 += static_cast<int>((v[(3 * t + 0) >> 2] >> (8 * ((3 * t + 0) & 3))) & 255u) * w[t];
+        a1 += static_cast<int>((v[(3 * t + 1) >> 2] >> (8 * ((3 * t + 1) & 3))) & 255u) * w[t];
+        a2 += static_cast<int>((v[(3 * t + 2) >> 2] >> (8 * ((3 * t + 2) & 3))) & 255u) * w[t];
       }
       uint8_t* dst = band + r * pitch + x;
       dst[0] = static_cast<uint8_t>(clip8(a0));
