@@ -63,6 +63,27 @@ int main(void) {
   expect(musc_b200_msm((const float*)(size_t)16, 1, 10, 8, 0, 1, (double*)(size_t)16,
                        (void*)(size_t)1024, (size_t)1 << 30, NULL) == MUSC_B200_ERR_INVALID,
          "msm N>=2");
+  /* pool-image preprocessing: size queries and contract violations */
+  expect(musc_b200_preprocess_workspace_bytes(900, 900, 518, 518, MUSC_B200_BICUBIC) >= (size_t)2 * 518 * 9 * 4,
+         "preprocess workspace");
+  expect(musc_b200_preprocess_workspace_bytes(900, 900, 36, 518, MUSC_B200_BICUBIC) == 0,
+         "preprocess workspace, 25x reduction");
+  expect(musc_b200_preprocess_workspace_bytes(900, 900, 518, 518, 7) == 0, "preprocess workspace, bad filter");
+  const float mean[3] = {0.5f, 0.5f, 0.5f}, zero_std[3] = {1.0f, 0.0f, 1.0f}, std3[3] = {0.2f, 0.2f, 0.2f};
+  expect(musc_b200_preprocess_images((const uint8_t*)(size_t)1024, 2, 900, 900, 900 * 900 * 3, 518, 518,
+                                     MUSC_B200_BICUBIC, mean, zero_std, MUSC_B200_F32, (void*)(size_t)1024,
+                                     (void*)(size_t)1024, 1 << 20, NULL) == MUSC_B200_ERR_INVALID,
+         "preprocess zero std");
+  expect(musc_b200_preprocess_images((const uint8_t*)(size_t)1024, 2, 900, 900, 100, 518, 518,
+                                     MUSC_B200_BICUBIC, mean, std3, MUSC_B200_F32, (void*)(size_t)1024,
+                                     (void*)(size_t)1024, 1 << 20, NULL) == MUSC_B200_ERR_INVALID,
+         "preprocess image stride");
+  expect(musc_b200_preprocess_images((const uint8_t*)(size_t)1024, 2, 900, 900, 900 * 900 * 3, 36, 518,
+                                     MUSC_B200_BICUBIC, mean, std3, MUSC_B200_F32, (void*)(size_t)1024,
+                                     (void*)(size_t)1024, 1 << 20, NULL) == MUSC_B200_ERR_INVALID,
+         "preprocess 25x reduction");
+  expect(strstr(musc_b200_last_error(), "15.75x") != NULL, "preprocess ratio message");
+
   int code = -1;
   expect(musc_b200_take_device_error(NULL) == MUSC_B200_ERR_INVALID, "device error null");
   (void)code;
