@@ -667,6 +667,16 @@ def run_images_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _img_traffic(n: int):
+    """DRAM bytes per launch of the resample kernel for ``n`` images, scaled from the committed
+    ncu capture (or None)."""
+    try:
+        d = json.loads((REPO / 'profiles' / 'resample_kernel_traffic.json').read_text())
+        return d['bytes_per_launch_pool200'] * n / 200
+    except Exception:
+        return None
+
+
 def run_images(args):
     """``value``: the device transform over a resident batch of ``--pool`` (default 200, the
     config-5 pool) 900 x 900 images (486 MB in, 644 MB out: no L2 flush needed); ``e2e``: the
@@ -731,9 +741,9 @@ def run_images(args):
             'e2e': {'value': n / e2e_s, 'unit': UNIT, 'h2d_bytes_per_step': int(host.nbytes),
                     'd2h_bytes_per_step': 0, 'note': 'host arrays -> pinned staging -> H2D -> kernels; '
                                                      'the result stays on the device for the encoder'},
-            'roofline': {'kernel': 'resample_kernel (+ tables_kernel)', 'bound': 'hbm', 'achieved': achieved,
+            'roofline': {'kernel': 'resample_staged_kernel (+ tables_kernel)', 'bound': 'hbm', 'achieved': achieved,
                          'peak': peaks['hbm_gbs'], 'unit': 'GB/s', 'frac': achieved / peaks['hbm_gbs'],
-                         'traffic': None, 'algorithmic_bytes_per_launch': algo_bytes,
+                         'traffic': _img_traffic(n), 'algorithmic_bytes_per_launch': algo_bytes,
                          'launch_ms': launch_ms, 'peak_kind': f'{peak_kind} HBM copy'},
             'gpu_launches': 2 * args.steps, 'clocks': clocks.summary(),
             'parity': {'images_checked': probe, 'bit_exact_vs_oracle': exact}}
