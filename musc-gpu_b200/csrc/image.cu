@@ -443,9 +443,17 @@ int launch(const Params& p, const Plan& plan, int n_images, cudaStream_t stream)
                                      : resample_kernel<OutT>;
   int threads = plan.staged_kh ? staged_threads(plan.staged_kh) : kThreads;
   MUSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem)));
-  dim3 grid((p.out_h + p.ty - 1) / p.ty, n_images);
-  kern<<<grid, threads, plan.smem, stream>>>(p);
-  return check_launch("resample_kernel");
+  // gridDim.y is at most 65535: larger batches go in slices of that many images
+  constexpr int kMaxGridY = 65535;
+  for (int first = 0; first < n_images; first += kMaxGridY) {
+    Params q = p;
+    q.images = p.images + static_cast<long long>(first) * p.image_stride;
+    q.out = static_cast<OutT*>(p.out) + static_cast<long long>(first) * 3 * p.out_h * p.out_w;
+    dim3 grid((p.out_h + p.ty - 1) / p.ty, min(kMaxGridY, n_images - first));
+    kern<<<grid, threads, plan.smem, stream>>>(q);
+    MUSC_TRY(check_launch("resample_kernel"));
+  }
+  return MUSC_B200_OK;
 }
 
 }  // namespace image
