@@ -623,7 +623,7 @@ def _img_pool(n: int, seed: int = 3):
     return rng.integers(0, 256, (n, IMG_H, IMG_W, 3), dtype=np.uint8)
 
 
-def images_cpu_measure(n_sample: int) -> dict:
+def images_cpu_measure(n_sample: int, min_seconds: float = 5.0) -> dict:
     """The reference's per-image transform (PIL bicubic resize, ToTensor, Normalize; the
     torchvision classes of ``open_clip/transform.py:124-133``) on ``n_sample`` images, one
     image per host thread as the reference's threaded loader runs them."""
@@ -636,14 +636,19 @@ def images_cpu_measure(n_sample: int) -> dict:
     torch.set_num_threads(1)
     tf = torch_cpu.clip_image_transform(IMG_OUT)
     pil = [Image.fromarray(a) for a in _img_pool(min(n_sample, 8), seed=4)]
+    done = 0
     with ThreadPoolExecutor(max_workers=cores) as ex:
         list(ex.map(tf, pil[:2]))
         t0 = time.perf_counter()
-        list(ex.map(tf, [pil[i % len(pil)] for i in range(n_sample)]))
-        wall = time.perf_counter() - t0
-    return {'value': n_sample / wall, 'cores': cores, 'wall_s': wall,
-            'sample': f'{n_sample} images of {IMG_H}x{IMG_W} through the torchvision/PIL transform, '
-                      f'{cores} threads, torch intra-op threads 1'}
+        while True:   # batches of n_sample images until at least min_seconds have passed
+            list(ex.map(tf, [pil[i % len(pil)] for i in range(n_sample)]))
+            done += n_sample
+            wall = time.perf_counter() - t0
+            if wall >= min_seconds:
+                break
+    return {'value': done / wall, 'cores': cores, 'wall_s': wall,
+            'sample': f'{done} images of {IMG_H}x{IMG_W} through the torchvision/PIL transform '
+                      f'({wall:.1f} s), {cores} threads, torch intra-op threads 1'}
 
 
 def run_images_reference(args):
@@ -652,7 +657,7 @@ def run_images_reference(args):
     n_sample = 4 * (os.cpu_count() or 1)
     ms = []
     for i in range(args.warmup + args.steps):
-        m = images_cpu_measure(n_sample)
+        m = images_cpu_measure(n_sample, min_seconds=1.0)
         if i >= args.warmup:
             ms.append(m)
     value = statistics.median(x['value'] for x in ms)
@@ -660,7 +665,7 @@ def run_images_reference(args):
             'warmup': args.warmup, 'ms_per_step': statistics.median(x['wall_s'] for x in ms) * 1e3,
             'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8 -> f32',
             'data': 'synthetic', 'impl': 'reference',
-            'config': {'workload': f'{n_sample} images per step (sample), {IMG_H}x{IMG_W} -> {IMG_OUT}'},
+            'config': {'workload': f'at least {n_sample} images and 1 s per step (sample), {IMG_H}x{IMG_W} -> {IMG_OUT}'},
             'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': ms[0]['cores'], 'kind': 'reference',
                              'sample': ms[0]['sample']},
             'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
