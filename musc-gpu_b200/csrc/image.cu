@@ -324,9 +324,10 @@ __global__ void __launch_bounds__(staged_threads(KH), 2) resample_staged_kernel(
       int a0 = 1 << (kPrecisionBits - 1), a1 = a0, a2 = a0;
 #pragma unroll
       for (int t = 0; t < KH; ++t) {
-        a0 += static_cast<int>((v[(3 * t + 0) >> 2] >> (8 * ((3 * t + 0) & 3))) & 255u) * w[t];
-        a1 += static_cast<int>((v[(3 * t + 1) >> 2] >> (8 * ((3 * t + 1) & 3))) & 255u) * w[t];
-        a2 += static_cast<int>((v[(3 * t + 2) >> 2] >> (8 * ((3 * t + 2) & 3))) & 255u) * w[t];
+        // byte j of the window: one byte permute (selector j & 3 for the low byte, 4 = zero)
+        a0 += static_cast<int>(__byte_perm(v[(3 * t + 0) >> 2], 0u, 0x4440u | ((3 * t + 0) & 3))) * w[t];
+        a1 += static_cast<int>(__byte_perm(v[(3 * t + 1) >> 2], 0u, 0x4440u | ((3 * t + 1) & 3))) * w[t];
+        a2 += static_cast<int>(__byte_perm(v[(3 * t + 2) >> 2], 0u, 0x4440u | ((3 * t + 2) & 3))) * w[t];
       }
       uint8_t* dst = band + r * pitch + x;
       dst[0] = static_cast<uint8_t>(clip8(a0));
