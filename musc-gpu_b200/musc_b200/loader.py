@@ -171,6 +171,16 @@ class DeviceImageLoader:
                 offset += size
         return out
 
+    def close(self) -> None:
+        """Wait for the staging copies in flight and stop the host copy threads."""
+        for ev in self._copied:
+            if ev is not None:
+                ev.synchronize()
+        if self._copier is not None:
+            self._copier.shutdown(wait=True)
+            self._copier = None
+            self._copy_stream = None
+
     def __iter__(self):
         for i, samples in enumerate(ordered_batches(self.dataset, self.batch_size, self.workers,
                                                     self.prefetch_batches)):

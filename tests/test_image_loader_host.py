@@ -62,6 +62,7 @@ def test_loader_checks_arguments_like_the_reference():
         DeviceImageLoader(_Items(3), device='cpu', filter='lanczos')
     loader = DeviceImageLoader(_Items(10), batch_size=4, device='cpu')
     assert len(loader) == 3
+    loader.close()   # nothing started: no-op
 
 
 def test_raw_rgb_converts_modes():
